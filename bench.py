@@ -1,0 +1,520 @@
+"""Benchmark of the B200 path: one JSON line per run.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gelu|rows|collatz]
+                    [--impl b200|reference]
+
+A step is one pass of the hot path over one batch of seeded synthetic input:
+
+* gelu    -- y = gelu_tanh(a*b + c) over three fp32 vectors of 2^24 elements (uniform
+             [-4, 4], seed 0): the fused elementwise group, through the module the b200
+             backend builds from tests/golden/gelu.ppyir. Metric: GB/s of algorithmic
+             traffic (16 B per element).
+* rows    -- softmax then layernorm over each row of an fp32 [65536, 1024] matrix
+             (N(0,1), seed 0; gamma ~ N(1, .02), beta ~ N(0, .02)): the row group built
+             from tests/golden/rows.ppyir. Metric: GB/s (8 B per element + gamma, beta).
+* collatz -- the step counts of every start in [1, 2^26) summed and maxed: the
+             parallel.reduce kernels built from tests/golden/collatz.ppyir. Metric:
+             Collatz steps per second.
+
+`value` is device-timed (CUDA events, inputs resident in HBM); `e2e` is the same metric
+through the host-memory C-ABI entry point (pinned host buffers, H2D and D2H inside the
+timed region). With --gpus N under torchrun each rank runs its own batch (weak scaling)
+or its slice of the Collatz range (strong), the time is the max over ranks.
+`--impl reference` times the oracle's C restatement of the reference's CPU loops on the
+host cores instead (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+PREBUILT = REPO / "ppy_b200" / "prebuilt"
+
+GELU_N = 1 << 24
+ROWS, COLS = 65536, 1024
+COLLATZ_HI = 1 << 26
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--workload", default="gelu", choices=["gelu", "rows", "collatz"])
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="CPU-baseline sample length (seconds of host work)")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------- distributed plumbing
+
+
+class Dist:
+    def __init__(self, gpus: int) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.gpus = gpus
+        self.pg = None
+
+    def start(self, backend: str) -> None:
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+            self.pg = dist
+
+    def barrier(self) -> None:
+        if self.pg is not None:
+            if self.pg.get_backend() == "nccl":
+                import torch
+
+                self.pg.barrier(device_ids=[self.local])
+                torch.cuda.synchronize()
+            else:
+                self.pg.barrier()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        import torch
+
+        device = "cuda" if self.pg.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_i64(self, values: list[int], op: str = "sum") -> list[int]:
+        if self.pg is None:
+            return values
+        import torch
+
+        device = "cuda" if self.pg.get_backend() == "nccl" else "cpu"
+        t = torch.tensor(values, dtype=torch.int64, device=device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM if op == "sum" else self.pg.ReduceOp.MAX)
+        return [int(v) for v in t.tolist()]
+
+    def stop(self) -> None:
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- clocks
+
+
+class Clocks:
+    """nvidia-smi samples (SM clock, throttle reasons) while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.samples: list[tuple[float, list[str]]] = []
+        self.window: tuple[float, float] | None = None
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                    timeout=5, check=False).stdout.strip()
+                if out:
+                    self.samples.append((time.perf_counter(), [x.strip() for x in out.split(",")]))
+            except (OSError, subprocess.SubprocessError):
+                return
+            self._stop.wait(0.05)
+
+    def start(self) -> None:
+        self._thread.start()
+
+    def mark(self, begin: float, end: float) -> None:
+        self.window = (begin, end)
+
+    def stop(self) -> dict:
+        self._stop.set()
+        self._thread.join(timeout=10)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        inside = [s for t, s in self.samples if self.window and self.window[0] <= t <= self.window[1]]
+        chosen = inside or [s for _, s in self.samples]
+        sm = sorted(float(s[1]) for s in chosen if s[1].replace(".", "").isdigit())
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in chosen:
+            for name, flag in zip(names, s[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
+                "sm_max_mhz": float(chosen[0][2]) if chosen[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(chosen),
+                "samples_in_timed_region": len(inside)}
+
+
+def peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    path = REPO / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(kernel)
+    return float(entry["bytes_per_launch"]) if entry else None
+
+
+# ---------------------------------------------------------------- workloads
+
+
+class Workload:
+    metric = ""
+    unit = ""
+    dtype = ""
+    kernel = ""
+    scaling = "weak"
+
+    def __init__(self, dist: Dist) -> None:
+        self.dist = dist
+
+
+class Gelu(Workload):
+    metric = "fused-group GB/s: y = gelu_tanh(a*b + c), fp32, 2^24 elements"
+    unit = "GB/s"
+    dtype = "f32"
+    kernel = "gelu_chain_k0_v"
+    bytes_per_step = 16 * GELU_N
+
+    def inputs(self):
+        rng = np.random.default_rng(0 + self.dist.rank)
+        self.host = [rng.uniform(-4, 4, GELU_N).astype(np.float32) for _ in range(3)]
+
+    def config(self):
+        return {"workload": "gelu_chain_f32", "elements": GELU_N, "seed": 0,
+                "bytes_per_step": self.bytes_per_step,
+                "l2": "inputs larger than L2 (201 MB read per step), no flush"}
+
+    def setup_device(self, runtime, torch):
+        self.module = runtime.load(PREBUILT / "gelu" / "gelu.json")
+        self.dev = [torch.from_numpy(x).cuda() for x in self.host]
+        self.out = torch.empty_like(self.dev[0])
+        self.pinned = [torch.from_numpy(x).pin_memory() for x in self.host]
+        self.pinned_out = torch.empty(GELU_N, dtype=torch.float32).pin_memory()
+
+    def step_device(self):
+        return self.module.device.gelu_chain(*self.dev, self.out).status
+
+    def step_host(self):
+        return self.module.gelu_chain(*self.pinned, self.pinned_out).status
+
+    def h2d_d2h(self):
+        return 12 * GELU_N, 4 * GELU_N
+
+    def cpu_step(self, threads: int, oracle):
+        # a bounded sample of the batch: the first 2^22 elements
+        n = 1 << 22
+        oracle.gelu_chain(self.host[0][:n], self.host[1][:n], self.host[2][:n], threads=threads)
+        return 16 * n
+
+    def check(self, oracle):
+        sample = slice(0, 1 << 16)
+        expected = oracle.gelu_chain(self.host[0][sample].copy(), self.host[1][sample].copy(),
+                                     self.host[2][sample].copy())
+        got = self.out[: 1 << 16].cpu().numpy()
+        scale = np.maximum(np.abs(expected), 1.0)
+        return float(np.max(np.abs(got - expected) / scale))
+
+
+class Rows(Workload):
+    metric = "fused-group GB/s: row softmax -> layernorm, fp32 [65536, 1024]"
+    unit = "GB/s"
+    dtype = "f32"
+    kernel = "softmax_layernorm_k0"
+    bytes_per_step = 2 * 4 * ROWS * COLS + 2 * 4 * COLS
+
+    def inputs(self):
+        rng = np.random.default_rng(0 + self.dist.rank)
+        self.x = rng.standard_normal((ROWS, COLS), dtype=np.float32)
+        self.gamma = (1 + 0.02 * rng.standard_normal(COLS)).astype(np.float32)
+        self.beta = (0.02 * rng.standard_normal(COLS)).astype(np.float32)
+
+    def config(self):
+        return {"workload": "softmax_layernorm_rows_f32", "rows": ROWS, "cols": COLS, "seed": 0,
+                "bytes_per_step": self.bytes_per_step,
+                "l2": "inputs larger than L2 (268 MB read per step), no flush"}
+
+    def setup_device(self, runtime, torch):
+        self.module = runtime.load(PREBUILT / "rows" / "rows.json")
+        self.dx = torch.from_numpy(self.x).cuda()
+        self.dg = torch.from_numpy(self.gamma).cuda()
+        self.db = torch.from_numpy(self.beta).cuda()
+        self.out = torch.empty_like(self.dx)
+        self.px = torch.from_numpy(self.x).pin_memory()
+        self.pout = torch.empty_like(self.px).pin_memory()
+
+    def step_device(self):
+        return self.module.device.softmax_layernorm(self.dx, self.dg, self.db, self.out).status
+
+    def step_host(self):
+        return self.module.softmax_layernorm(self.px.view(-1), torch_from(self.gamma),
+                                             torch_from(self.beta), self.pout.view(-1)).status
+
+    def h2d_d2h(self):
+        return 4 * ROWS * COLS + 8 * COLS, 4 * ROWS * COLS
+
+    def cpu_step(self, threads: int, oracle):
+        rows = 4096
+        oracle.softmax_layernorm(self.x[:rows], self.gamma, self.beta, threads=threads)
+        return 2 * 4 * rows * COLS
+
+    def check(self, oracle):
+        expected = oracle.softmax_layernorm(self.x[:256].copy(), self.gamma, self.beta)
+        got = self.out[:256].cpu().numpy()
+        return float(np.max(np.abs(got - expected) / np.maximum(np.abs(expected), 1.0)))
+
+
+def torch_from(array):
+    import torch
+
+    return torch.from_numpy(array)
+
+
+class Collatz(Workload):
+    metric = "Collatz steps/s: parallel.range(1, 2^26) int64 sum and max of step counts"
+    unit = "steps/s"
+    dtype = "int64"
+    kernel = "par_collatz_collatz_sum_0_part"
+    scaling = "strong"
+
+    def inputs(self):
+        world, rank = self.dist.world, self.dist.rank
+        span = (COLLATZ_HI - 1 + world - 1) // world
+        self.lo = 1 + rank * span
+        self.hi = min(COLLATZ_HI, self.lo + span)
+        self.total_steps = None
+
+    def config(self):
+        return {"workload": "collatz_parallel_range", "range": [1, COLLATZ_HI],
+                "rank_range": [self.lo, self.hi], "l2": "no data: integer-issue bound"}
+
+    def setup_device(self, runtime, torch):
+        self.module = runtime.load(PREBUILT / "collatz" / "collatz.json")
+
+    def step_device(self):
+        status, self.sum = self.module.device.ppy_collatz_collatz_sum(self.lo, self.hi)
+        status2, self.best = self.module.device.ppy_collatz_collatz_max(self.lo, self.hi)
+        return status or status2
+
+    step_host = step_device
+
+    def h2d_d2h(self):
+        return 32, 16  # (lo, hi) twice in, (sum, max) out
+
+    def cpu_step(self, threads: int, oracle):
+        hi = min(self.hi, self.lo + (1 << 22))
+        status, total, _best = oracle.collatz(self.lo, hi, threads)
+        return total
+
+    def check(self, oracle):
+        return 0.0
+
+
+WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz}
+
+
+def units_per_step(w: Workload) -> float:
+    if isinstance(w, Collatz):
+        if w.total_steps is None:
+            w.total_steps = w.sum
+        return float(w.total_steps)
+    return float(w.bytes_per_step)
+
+
+def to_metric(w: Workload, units: float, seconds: float) -> float:
+    if w.unit == "GB/s":
+        return units / seconds / 1e9
+    return units / seconds
+
+
+def cpu_baseline(w: Workload, seconds: float) -> dict:
+    import oracle
+
+    threads = oracle.threads_available()
+    done = 0.0
+    start = time.perf_counter()
+    steps = 0
+    while True:
+        done += w.cpu_step(threads, oracle)
+        steps += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds:
+            break
+    sample = {"gelu": "first 2^22 elements of the batch, repeated",
+              "rows": "first 4096 rows of the batch, repeated",
+              "collatz": "starts [lo, lo + 2^22) of the range, repeated"}[
+        next(k for k, v in WORKLOADS.items() if isinstance(w, v))]
+    return {"value": to_metric(w, done, elapsed), "unit": w.unit, "cores": threads,
+            "kind": "port", "sample": f"{sample}; {steps} passes in {elapsed:.1f} s"}
+
+
+def run_reference(args, dist: Dist) -> None:
+    dist.start("gloo")
+    if dist.rank != 0:
+        dist.stop()
+        return
+    w = WORKLOADS[args.workload](dist)
+    w.dist.world = 1
+    w.inputs()
+    import oracle
+
+    threads = oracle.threads_available()
+    for _ in range(args.warmup):
+        w.cpu_step(threads, oracle)
+    units = 0.0
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        units += w.cpu_step(threads, oracle)
+    elapsed = time.perf_counter() - start
+    value = to_metric(w, units, elapsed)
+    line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed / max(args.steps, 1) * 1e3, "higher_is_better": True,
+            "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+            "config": w.config(), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": w.unit, "cores": threads, "kind": "port",
+                             "sample": "one bounded sample of the batch per step (oracle C "
+                                       "restatement of the reference's CPU loops, OpenMP)"},
+            "e2e": {"value": value, "unit": w.unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    dist.stop()
+
+
+def run_b200(args, dist: Dist) -> None:
+    import torch
+
+    from ppy_b200 import runtime
+
+    torch.cuda.set_device(dist.local)
+    dist.start("nccl")
+    runtime.init(dist.local)
+    stream = torch.cuda.current_stream()
+    runtime.set_stream(stream)
+    w = WORKLOADS[args.workload](dist)
+    w.inputs()
+    w.setup_device(runtime, torch)
+    clocks = Clocks(dist.local)
+    clocks.start()
+    for _ in range(max(args.warmup, 3)):
+        assert w.step_device() == 0
+        assert w.step_host() == 0
+    torch.cuda.synchronize()
+    # device-resident timing: one event pair around every step
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = runtime.launches()
+    dist.barrier()
+    torch.cuda.synchronize()
+    begin = time.perf_counter()
+    for i in range(args.steps):
+        starts[i].record(stream)
+        status = w.step_device()
+        ends[i].record(stream)
+        if status != 0:
+            raise SystemExit(f"step failed with status {status}")
+    torch.cuda.synchronize()
+    dist.barrier()
+    end = time.perf_counter()
+    clocks.mark(begin, end)
+    launches = runtime.launches() - launches0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = starts[0].elapsed_time(ends[-1])
+    total_ms = dist.max(total_ms)
+    units = units_per_step(w)
+    units_all = units * (dist.world if w.scaling == "weak" else 1)
+    if isinstance(w, Collatz):
+        sums = dist.sum_i64([w.sum])
+        units_all = float(sums[0])
+    value = to_metric(w, units_all * args.steps, total_ms / 1e3)
+    kernel_ms = float(np.mean(step_ms))
+    # end to end through the host-memory entry point (pinned host buffers)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    launches1 = runtime.launches()
+    e_start.record(stream)
+    for _ in range(args.steps):
+        if w.step_host() != 0:
+            raise SystemExit("host-memory step failed")
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    launches += runtime.launches() - launches1
+    e2e_ms = dist.max(e_start.elapsed_time(e_end))
+    e2e = to_metric(w, units_all * args.steps, e2e_ms / 1e3)
+    clock_info = clocks.stop()
+    import oracle
+
+    error = w.check(oracle)
+    if dist.rank == 0:
+        pk = peaks()
+        h2d, d2h = w.h2d_d2h()
+        line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": dist.world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+                "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None,
+                "dtype": w.dtype, "data": "synthetic (seeded)", "config": w.config(),
+                "e2e": {"value": e2e, "unit": w.unit, "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h},
+                "gpu_launches": int(launches), "clocks": clock_info,
+                "max_rel_error_vs_oracle": error}
+        if w.unit == "GB/s":
+            achieved = w.bytes_per_step / (kernel_ms / 1e3) / 1e9
+            line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                                "traffic": traffic(w.kernel), "peak_source": pk["source"],
+                                "kernel": w.kernel, "kernel_ms": kernel_ms}
+        else:
+            line["roofline"] = {"bound": "int-issue", "achieved": value, "peak": None,
+                                "unit": w.unit, "frac": None, "traffic": None,
+                                "kernel": w.kernel, "kernel_ms": kernel_ms}
+        if dist.world == 1:
+            line["cpu_baseline"] = cpu_baseline(w, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    dist.stop()
+
+
+def main() -> None:
+    args = _args()
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, dist)
+    else:
+        run_b200(args, dist)
+
+
+if __name__ == "__main__":
+    main()

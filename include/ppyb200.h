@@ -1,0 +1,111 @@
+/* ppyb200.h -- the C ABI of the PPy B200 backend.
+ *
+ * Two kinds of entry points live behind this ABI.
+ *
+ * 1. libppyb200.so, the runtime every built module uses: device selection, the
+ *    launch stream, the per-device scratch arena and status word, cached device
+ *    buffers for host-memory calls, and the hand-written kernels that are not
+ *    generated per module (the dense matmul, the Collatz-style range reduction).
+ *
+ * 2. The per-module libraries `ppy build X --backend b200` writes. Each IR function
+ *    F of a built module exports
+ *
+ *        int32_t <symbol>(<atoms of each parameter>..., int64_t *slot);
+ *        int32_t <symbol>__device(<atoms of each parameter>..., int64_t *slot);
+ *
+ *    with the atoms of the reference's native ABI (backend/llvm/from_ir.py:1-13,
+ *    the signature tests/test_tensor_fusion.py:269-282 calls through ctypes): a
+ *    `buffer<T>` parameter is `T *data, int64_t len`; an `f64`/`f32` scalar is a
+ *    `double`/`float`; an `i64` is `int64_t`; a `ptr<T>` is `T *`; the function's
+ *    result is written to `*slot`. `<symbol>` takes HOST buffers (it copies what the
+ *    function reads to the device, launches, and copies what it writes back);
+ *    `<symbol>__device` takes DEVICE buffers and launches on the current stream.
+ *    Both return the reference's status (ppy_runtime/abi.py:25-35):
+ *    PPYB200_OK, PPYB200_FALLBACK (a guard failed: the caller reruns the function
+ *    in CPython, as it does for the LLVM backend), or PPYB200_RAISED (a CUDA error;
+ *    ppyb200_last_error() says which).
+ *
+ * Every function here is thread-safe; the device and stream are per calling thread.
+ */
+#ifndef PPYB200_H
+#define PPYB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PPYB200_ABI_VERSION 1
+
+/* ppy_runtime/abi.py:25-35: STATUS_OK, STATUS_FALLBACK, STATUS_RAISED. */
+#define PPYB200_OK 0
+#define PPYB200_FALLBACK 1
+#define PPYB200_RAISED (-1)
+
+/* ---------------------------------------------------------------- runtime */
+
+/* The ABI version this library implements (PPYB200_ABI_VERSION). */
+int32_t ppyb200_abi_version(void);
+
+/* Number of CUDA devices visible, or 0 without a driver or a device. Replaces the
+ * device probe of ppy_runtime/cuda.py:146-163 (`available`). */
+int32_t ppyb200_device_count(void);
+
+/* Make `device` the calling thread's device (cudaSetDevice) and create its state.
+ * Replaces ppy_runtime/cuda.py:51-57 (`Driver` binds device 0's primary context);
+ * here every device of the node may be bound, one per calling thread. */
+int32_t ppyb200_init(int32_t device);
+
+/* The calling thread's device, or -1 before ppyb200_init. */
+int32_t ppyb200_current_device(void);
+
+/* The message of the calling thread's last failure ("" when none). Replaces
+ * ppy_runtime/cuda.py:36-38 (`CudaError` carries the driver's error string). */
+const char *ppyb200_last_error(void);
+
+/* Record a failure message for the calling thread (used by built modules). */
+void ppyb200_set_error(const char *message);
+
+/* The stream the calling thread's launches go to: a cudaStream_t, or NULL for the
+ * current device's own non-blocking stream. */
+int32_t ppyb200_set_stream(void *stream);
+void *ppyb200_stream(void);
+
+/* Wait for the calling thread's stream. */
+int32_t ppyb200_sync(void);
+
+/* Number of streaming multiprocessors of the current device. */
+int32_t ppyb200_sm_count(void);
+
+/* Device memory that a call may use as temporaries, reused by the next call on the
+ * same (device, stream): at least `bytes`, 256-byte aligned, NULL on failure. */
+void *ppyb200_scratch(int64_t bytes);
+
+/* A zeroed device int32 status word for one call on the current stream (the
+ * zeroing is enqueued on that stream). Kernels raise it to PPYB200_FALLBACK. */
+int32_t *ppyb200_status_word(void);
+
+/* Read the status word back after the call's kernels (synchronises the stream). */
+int32_t ppyb200_read_status(int32_t *word);
+
+/* Cached device buffers for host-memory calls. */
+void *ppyb200_device_buffer(int64_t bytes);
+void ppyb200_release_buffer(void *pointer);
+
+/* Host<->device copies on the current stream (async; ppyb200_sync waits). */
+int32_t ppyb200_copy_to_device(void *device_dst, const void *host_src, int64_t bytes);
+int32_t ppyb200_copy_to_host(void *host_dst, const void *device_src, int64_t bytes);
+
+/* Translate a cudaError_t into a status, recording `what` when it is a failure. */
+int32_t ppyb200_check(int32_t cuda_error, const char *what);
+
+/* Kernels launched through this library and the modules built against it. */
+uint64_t ppyb200_launches(void);
+void ppyb200_count_launches(uint64_t count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PPYB200_H */

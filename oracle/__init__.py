@@ -1,0 +1,149 @@
+"""ORACLE -- test infrastructure only.
+
+The checker the parity tests, `__graft_entry__.smoke()` and bench.py's CPU-baseline leg
+compare the B200 path against. Nothing under `ppy_b200/` imports it. It is a
+restatement of the reference's CPU semantics for the hot path (`ref_loops.c`, with
+the file:line of each rule it follows), compiled by `oracle/Makefile`, pinned against
+the reference's own outputs in tests/golden/ (tests/test_oracle_golden.py).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIBRARY = HERE / "_build" / "liboracle.so"
+
+_lock = threading.Lock()
+_lib = None
+
+STATUS_OK = 0
+STATUS_FALLBACK = 1
+
+
+def build() -> Path:
+    """Compile ref_loops.c (gcc, OpenMP) into oracle/_build/liboracle.so."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIBRARY
+
+
+def _library():
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIBRARY.exists() or LIBRARY.stat().st_mtime < (HERE / "ref_loops.c").stat().st_mtime:
+                build()
+            lib = ctypes.CDLL(str(LIBRARY))
+            f32p = ctypes.POINTER(ctypes.c_float)
+            i64 = ctypes.c_int64
+            lib.oracle_gelu_chain.argtypes = [f32p, f32p, f32p, f32p, i64]
+            lib.oracle_gelu_chain_omp.argtypes = [f32p, f32p, f32p, f32p, i64, ctypes.c_int]
+            lib.oracle_softmax_layernorm.argtypes = [f32p, f32p, f32p, f32p, i64, i64, f32p]
+            lib.oracle_softmax_layernorm_omp.argtypes = [f32p, f32p, f32p, f32p, i64, i64, f32p,
+                                                         ctypes.c_int]
+            lib.oracle_matmul_bias.argtypes = [f32p, f32p, f32p, f32p, i64, i64, i64]
+            lib.oracle_collatz.argtypes = [i64, i64, ctypes.POINTER(i64), ctypes.POINTER(i64),
+                                           ctypes.c_int]
+            lib.oracle_collatz.restype = ctypes.c_int
+            lib.oracle_collatz_steps.argtypes = [i64, i64, ctypes.POINTER(i64)]
+            lib.oracle_collatz_steps.restype = ctypes.c_int
+            _lib = lib
+        return _lib
+
+
+def _f32(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def threads_available() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1
+
+
+def gelu_chain(a, b, c, threads: int | None = None) -> np.ndarray:
+    out = np.empty_like(a)
+    if threads is None:
+        _library().oracle_gelu_chain(_f32(a), _f32(b), _f32(c), _f32(out), a.size)
+    else:
+        _library().oracle_gelu_chain_omp(_f32(a), _f32(b), _f32(c), _f32(out), a.size, threads)
+    return out
+
+
+def softmax_layernorm(x, gamma, beta, threads: int | None = None) -> np.ndarray:
+    rows, cols = x.shape
+    out = np.empty_like(x)
+    if threads is None:
+        work = np.empty(2 * cols, np.float32)
+        _library().oracle_softmax_layernorm(_f32(x), _f32(gamma), _f32(beta), _f32(out), rows,
+                                            cols, _f32(work))
+    else:
+        work = np.empty(2 * cols * max(threads, 1), np.float32)
+        _library().oracle_softmax_layernorm_omp(_f32(x), _f32(gamma), _f32(beta), _f32(out), rows,
+                                                cols, _f32(work), threads)
+    return out
+
+
+def matmul_bias(a, b, bias) -> np.ndarray:
+    m, k = a.shape
+    n = b.shape[1]
+    out = np.empty((m, n), np.float32)
+    _library().oracle_matmul_bias(_f32(a), _f32(b), _f32(bias) if bias is not None else None,
+                                  _f32(out), m, n, k)
+    return out
+
+
+def collatz(lo: int, hi: int, threads: int = 1) -> tuple[int, int, int]:
+    """(status, sum of steps, max of steps) over [lo, hi)."""
+    total, best = ctypes.c_int64(0), ctypes.c_int64(0)
+    status = _library().oracle_collatz(lo, hi, ctypes.byref(total), ctypes.byref(best), threads)
+    return status, total.value, best.value
+
+
+def collatz_steps(lo: int, hi: int) -> tuple[int, np.ndarray]:
+    out = np.zeros(max(hi - lo, 0), np.int64)
+    status = _library().oracle_collatz_steps(
+        lo, hi, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)))
+    return status, out
+
+
+# -- NumPy restatements for the small f64/f32 fixtures ----------------------------------------
+
+
+def ext_max(a, c):
+    """tensor.scalar_extremum max (ir/dialects/tensor.py:684-701): a NaN operand wins."""
+    chosen = np.where(a >= c, a, c)
+    return np.where(a == a, chosen, a)
+
+
+def ext_min(a, c):
+    chosen = np.where(a <= c, a, c)
+    return np.where(a == a, chosen, a)
+
+
+def fold(values: np.ndarray, kind: str, axis: int, dtype) -> np.ndarray:
+    """The reference's row-major fold from the identity (lower_tensor.py:733-754)."""
+    values = np.moveaxis(np.asarray(values, dtype), axis, 0)
+    if kind == "add":
+        acc = np.zeros(values.shape[1:], dtype)
+    elif kind == "mul":
+        acc = np.ones(values.shape[1:], dtype)
+    elif kind == "max":
+        acc = np.full(values.shape[1:], -np.inf, dtype)
+    else:
+        acc = np.full(values.shape[1:], np.inf, dtype)
+    for item in values:
+        if kind == "add":
+            acc = (acc + item).astype(dtype)
+        elif kind == "mul":
+            acc = (acc * item).astype(dtype)
+        elif kind == "max":
+            acc = ext_max(acc, item)
+        else:
+            acc = ext_min(acc, item)
+    return acc
