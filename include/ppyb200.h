@@ -86,7 +86,9 @@ void *ppyb200_scratch(int64_t bytes);
  * zeroing is enqueued on that stream). Kernels raise it to PPYB200_FALLBACK. */
 int32_t *ppyb200_status_word(void);
 
-/* Read the status word back after the call's kernels (synchronises the stream). */
+/* Read the status word back after the call's kernels (synchronises the stream):
+ * PPYB200_OK, PPYB200_FALLBACK, or PPYB200_RAISED when a device function raised (a
+ * loop of a parallel body past its trip bound, PPYB200_LOOP_LIMIT trips per index). */
 int32_t ppyb200_read_status(int32_t *word);
 
 /* Cached device buffers for host-memory calls. */

@@ -1044,8 +1044,9 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
              "t += (int64_t)gridDim.x * blockDim.x) {",
              "    const int64_t i = begin + t;",
              f"    {rt} next;",
-             f"    if ({k.body}(" + ", ".join(cap_names + ["i", "i + 1", "acc", "&next"]) + ") != PPY_STATUS_OK) {",
-             "      ppyb200::raise_fallback(status);",
+             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "i + 1", "acc", "&next"]) + ");",
+             "    if (s != PPY_STATUS_OK) {",
+             "      ppyb200::raise_status(status, s);",
              "      break;",
              "    }",
              "    acc = next;",
@@ -1093,8 +1094,9 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
              "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < count; "
              "t += (int64_t)gridDim.x * blockDim.x) {",
              "    const int64_t i = begin + t;",
-             f"    if ({k.body}(" + ", ".join(cap_names + ["i", "i + 1"]) + ") != PPY_STATUS_OK) {",
-             "      ppyb200::raise_fallback(status);", "      break;", "    }", "  }", "}"]
+             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "i + 1"]) + ");",
+             "    if (s != PPY_STATUS_OK) {",
+             "      ppyb200::raise_status(status, s);", "      break;", "    }", "  }", "}"]
         extra_params, extra_args = [], []
     else:  # map
         ot = P.ctype(k.out_dtype)
@@ -1105,8 +1107,9 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
              "t += (int64_t)gridDim.x * blockDim.x) {",
              "    const int64_t i = begin + t;",
              f"    {ot} value;",
-             f"    if ({k.body}(" + ", ".join(cap_names + ["i", "&value"]) + ") != PPY_STATUS_OK) {",
-             "      ppyb200::raise_fallback(status);", "      break;", "    }",
+             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "&value"]) + ");",
+             "    if (s != PPY_STATUS_OK) {",
+             "      ppyb200::raise_status(status, s);", "      break;", "    }",
              "    out[i] = value;", "  }", "}"]
         extra_params, extra_args = [f"{ot}* out"], ["out"]
     src.kernels.append("\n".join(L))

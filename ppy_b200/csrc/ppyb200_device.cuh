@@ -23,6 +23,15 @@
 #define PPY_STATUS_FALLBACK 1
 #define PPY_STATUS_RAISED (-1)
 
+// Status words kernels raise (atomicMax: the most severe wins). A body that failed with
+// PPY_STATUS_RAISED -- e.g. a loop past PPYB200_LOOP_LIMIT trips -- records
+// PPYB200_DEVICE_RAISED; the host maps it to PPY_STATUS_RAISED with a message.
+#define PPYB200_DEVICE_FALLBACK 1
+#define PPYB200_DEVICE_RAISED 2
+#ifndef PPYB200_LOOP_LIMIT
+#define PPYB200_LOOP_LIMIT (1u << 26)
+#endif
+
 namespace ppyb200 {
 
 // ---------------------------------------------------------------- min / max
@@ -136,7 +145,13 @@ __device__ __forceinline__ double logit(double x) { return log(x / (1.0 - x)); }
 
 // Record a fallback in the call's status word; the host wrapper reads it after the launch.
 __device__ __forceinline__ void raise_fallback(int32_t* status) {
-  if (status != nullptr) atomicMax(status, PPY_STATUS_FALLBACK);
+  if (status != nullptr) atomicMax(status, PPYB200_DEVICE_FALLBACK);
+}
+// Record the status a device function returned (fallback or raised).
+__device__ __forceinline__ void raise_status(int32_t* status, int32_t returned) {
+  if (status != nullptr)
+    atomicMax(status, returned == PPY_STATUS_FALLBACK ? PPYB200_DEVICE_FALLBACK
+                                                      : PPYB200_DEVICE_RAISED);
 }
 
 }  // namespace ppyb200

@@ -215,6 +215,10 @@ int32_t ppyb200_read_status(int32_t* word) {
   if (status != PPYB200_OK) return status;
   status = check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
   if (status != PPYB200_OK) return status;
+  // Kernels raise 1 (a guard failed: fall back) or 2 (a device function raised, e.g.
+  // a loop past its trip bound).
+  if (*host >= 2)
+    return fail("a device function raised: a loop passed its trip bound or a call failed");
   return *host;
 }
 

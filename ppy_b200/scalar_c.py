@@ -180,12 +180,27 @@ class _FunctionEmitter:
             for argument in block.arguments:
                 if block is not blocks[0]:
                     self.name(argument)
+        # Device code bounds every loop: a header reached more than PPYB200_LOOP_LIMIT
+        # times in one call returns PPY_STATUS_RAISED instead of spinning forever (a
+        # body such as Collatz never ends for a start <= 0, on the CPU as here).
+        index = {id(b): i for i, b in enumerate(blocks)}
+        headers = set()
+        if self.device:
+            for i, block in enumerate(blocks):
+                terminator = block.operations[-1] if block.operations else None
+                for successor in getattr(terminator, "successors", []) or []:
+                    if index[id(successor.block)] <= i:
+                        headers.add(id(successor.block))
         body: list[str] = []
         for block in blocks:
             body.append(f"{self.labels[id(block)]}:;")
+            if id(block) in headers:
+                body.append("  if (++loop_trips > PPYB200_LOOP_LIMIT) return PPY_STATUS_RAISED;")
             for op in block.operations:
                 body.extend("  " + line for line in self.op(op))
         text = [head + " {"]
+        if headers:
+            text.append("  uint32_t loop_trips = 0;")
         text += ["  " + d for d in self.decls]
         text += ["  " + c for c in entry_copies]
         text += [f"  goto {self.labels[id(blocks[0])]};"]

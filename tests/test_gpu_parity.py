@@ -231,3 +231,13 @@ def test_collatz_large_range_against_the_oracle(rt):
     assert status == 0
     assert tuple(module.ppy_collatz_collatz_sum(1, hi)) == (0, total)
     assert tuple(module.ppy_collatz_collatz_max(1, hi)) == (0, best)
+
+
+def test_a_body_that_never_ends_raises_instead_of_hanging(rt):
+    """Collatz from 0 never reaches 1 (the reference spins forever on the CPU); the
+    device copy of the body stops at its loop bound and the call raises."""
+    module = _load(rt, "collatz")
+    with pytest.raises(rt.B200Error, match="trip bound"):
+        module.ppy_collatz_collatz_sum(0, 1)
+    g = json.loads((GOLDEN / "collatz.json").read_text())
+    assert tuple(module.ppy_collatz_collatz_sum(1, 1000)) == (0, g["sum_1_1000"])
