@@ -117,7 +117,7 @@ class Dist:
 
 
 class Clocks:
-    """nvidia-smi samples (SM clock, throttle reasons) while the timed region runs."""
+    """nvidia-smi samples every 20 ms (SM clock, throttle reasons) around the timed region."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -127,36 +127,50 @@ class Clocks:
         self.device = device
         self.samples: list[tuple[float, list[str]]] = []
         self.window: tuple[float, float] | None = None
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._run, daemon=True)
+        self.process = None
+        self._thread = threading.Thread(target=self._read, daemon=True)
 
-    def _run(self) -> None:
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(
-                    ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
-                     "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                    timeout=5, check=False).stdout.strip()
-                if out:
-                    self.samples.append((time.perf_counter(), [x.strip() for x in out.split(",")]))
-            except (OSError, subprocess.SubprocessError):
-                return
-            self._stop.wait(0.05)
+    def _read(self) -> None:
+        for line in self.process.stdout:
+            fields = [x.strip() for x in line.split(",")]
+            if len(fields) >= 9:
+                self.samples.append((time.perf_counter(), fields))
 
     def start(self) -> None:
-        self._thread.start()
+        try:
+            self.process = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._thread.start()
+        except OSError:
+            self.process = None
 
     def mark(self, begin: float, end: float) -> None:
         self.window = (begin, end)
 
     def stop(self) -> dict:
-        self._stop.set()
-        self._thread.join(timeout=10)
+        if self.process is not None:
+            time.sleep(0.05)
+            self.process.terminate()
+            try:
+                self.process.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.process.kill()
+            self._thread.join(timeout=5)
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        inside = [s for t, s in self.samples if self.window and self.window[0] <= t <= self.window[1]]
+        inside = [s for t, s in self.samples
+                  if self.window and self.window[0] - 0.02 <= t <= self.window[1] + 0.02]
         chosen = inside or [s for _, s in self.samples]
-        sm = sorted(float(s[1]) for s in chosen if s[1].replace(".", "").isdigit())
+
+        def number(text):
+            try:
+                return float(text)
+            except ValueError:
+                return None
+
+        sm = sorted(v for v in (number(s[1]) for s in chosen) if v is not None)
         reasons = set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for s in chosen:
@@ -164,9 +178,8 @@ class Clocks:
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": sm[len(sm) // 2] if sm else None,
-                "sm_max_mhz": float(chosen[0][2]) if chosen[0][2].replace(".", "").isdigit() else None,
-                "reasons": sorted(reasons), "samples": len(chosen),
-                "samples_in_timed_region": len(inside)}
+                "sm_max_mhz": number(chosen[0][2]), "reasons": sorted(reasons),
+                "samples": len(chosen), "samples_in_timed_region": len(inside)}
 
 
 def peaks() -> dict:
@@ -324,8 +337,8 @@ class Collatz(Workload):
         self.module = runtime.load(PREBUILT / "collatz" / "collatz.json")
 
     def step_device(self):
-        status, self.sum = self.module.device.ppy_collatz_collatz_sum(self.lo, self.hi)
-        status2, self.best = self.module.device.ppy_collatz_collatz_max(self.lo, self.hi)
+        status, self.sum = self.module.device.collatz_collatz_sum(self.lo, self.hi)
+        status2, self.best = self.module.device.collatz_collatz_max(self.lo, self.hi)
         return status or status2
 
     step_host = step_device
@@ -421,7 +434,9 @@ def run_b200(args, dist: Dist) -> None:
     torch.cuda.set_device(dist.local)
     dist.start("nccl")
     runtime.init(dist.local)
-    stream = torch.cuda.current_stream()
+    # one stream for everything: the module's launches, copies and the timing events
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     runtime.set_stream(stream)
     w = WORKLOADS[args.workload](dist)
     w.inputs()

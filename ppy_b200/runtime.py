@@ -84,10 +84,19 @@ def init(device: int = 0) -> None:
         raise B200Error(f"device {device}: {last_error()}")
 
 
+#: cudaStreamLegacy: the default stream, spelled so that it is not mistaken for "none".
+_LEGACY_STREAM = 0x1
+
+
 def set_stream(stream) -> None:
-    """Launch this thread's calls on `stream` (a torch.cuda.Stream, a raw handle, or None)."""
-    handle = getattr(stream, "cuda_stream", stream)
-    library().ppyb200_set_stream(ctypes.c_void_p(int(handle) if handle else 0))
+    """Launch this thread's calls on `stream`: a torch.cuda.Stream or a raw cudaStream_t
+    handle (torch's default stream, handle 0, is the legacy default stream), or None for
+    the runtime's own non-blocking stream of the device."""
+    if stream is None:
+        library().ppyb200_set_stream(ctypes.c_void_p(0))
+        return
+    handle = int(getattr(stream, "cuda_stream", stream) or 0)
+    library().ppyb200_set_stream(ctypes.c_void_p(handle or _LEGACY_STREAM))
 
 
 def launches() -> int:

@@ -29,7 +29,8 @@ def rt():
     if not torch.cuda.is_available():
         pytest.fail("a GPU test ran without a CUDA device")
     runtime.init(0)
-    runtime.set_stream(None)
+    # torch's current stream: the tests' copies and the module's kernels stay in order
+    runtime.set_stream(torch.cuda.current_stream())
     return runtime
 
 
@@ -196,28 +197,28 @@ def test_large_reductions_against_the_oracle(rt):
 def test_collatz_matches_ppy_run(rt):
     module = _load(rt, "collatz")
     g = json.loads((GOLDEN / "collatz.json").read_text())
-    assert tuple(module.ppy_collatz_collatz_sum(1, 1 << 16)) == (0, g["sum_1_65536"])
-    assert tuple(module.ppy_collatz_collatz_sum(1, 1000)) == tuple(g["jit_sum_1_1000"])
-    assert tuple(module.ppy_collatz_collatz_sum(27, 28)) == (0, g["sum_27_28"])
-    assert tuple(module.ppy_collatz_collatz_sum(5, 5)) == (0, g["sum_5_5"])
-    assert tuple(module.ppy_collatz_collatz_max(1, 4096)) == tuple(g["jit_max_1_4096"])
-    assert tuple(module.ppy_collatz_collatz_max(1, 1 << 16)) == tuple(g["jit_max_1_65536"])
+    assert tuple(module.collatz_collatz_sum(1, 1 << 16)) == (0, g["sum_1_65536"])
+    assert tuple(module.collatz_collatz_sum(1, 1000)) == tuple(g["jit_sum_1_1000"])
+    assert tuple(module.collatz_collatz_sum(27, 28)) == (0, g["sum_27_28"])
+    assert tuple(module.collatz_collatz_sum(5, 5)) == (0, g["sum_5_5"])
+    assert tuple(module.collatz_collatz_max(1, 4096)) == tuple(g["jit_max_1_4096"])
+    assert tuple(module.collatz_collatz_max(1, 1 << 16)) == tuple(g["jit_max_1_65536"])
 
 
 def test_collatz_overflow_takes_the_fallback(rt):
     module = _load(rt, "collatz")
     g = json.loads((GOLDEN / "collatz.json").read_text())
     lo, hi = g["overflow_range"]
-    assert module.ppy_collatz_collatz_sum(lo, hi).status == g["jit_overflow_status"] == 1
+    assert module.collatz_collatz_sum(lo, hi).status == g["jit_overflow_status"] == 1
     # the status word is per call: the next call is clean
-    assert tuple(module.ppy_collatz_collatz_sum(1, 1000)) == (0, g["sum_1_1000"])
+    assert tuple(module.collatz_collatz_sum(1, 1000)) == (0, g["sum_1_1000"])
 
 
 def test_collatz_steps_parallel_for_writes_device_memory(rt):
     module = _load(rt, "collatz")
     g = json.loads((GOLDEN / "collatz.json").read_text())
     out = torch.zeros(4095, dtype=torch.int64, device="cuda")
-    status, count = module.ppy_collatz_collatz_steps(out, 1, 4096)
+    status, count = module.collatz_collatz_steps(out, 1, 4096)
     assert (status, count) == (0, g["steps_count_1_4096"])
     steps = out.cpu().numpy()
     assert steps[26] == g["steps_of_27"] and steps.max() == g["max_1_4096"]
@@ -229,8 +230,8 @@ def test_collatz_large_range_against_the_oracle(rt):
     hi = 1 << 24
     status, total, best = oracle.collatz(1, hi, oracle.threads_available())
     assert status == 0
-    assert tuple(module.ppy_collatz_collatz_sum(1, hi)) == (0, total)
-    assert tuple(module.ppy_collatz_collatz_max(1, hi)) == (0, best)
+    assert tuple(module.collatz_collatz_sum(1, hi)) == (0, total)
+    assert tuple(module.collatz_collatz_max(1, hi)) == (0, best)
 
 
 def test_a_body_that_never_ends_raises_instead_of_hanging(rt):
@@ -238,6 +239,6 @@ def test_a_body_that_never_ends_raises_instead_of_hanging(rt):
     device copy of the body stops at its loop bound and the call raises."""
     module = _load(rt, "collatz")
     with pytest.raises(rt.B200Error, match="trip bound"):
-        module.ppy_collatz_collatz_sum(0, 1)
+        module.collatz_collatz_sum(0, 1)
     g = json.loads((GOLDEN / "collatz.json").read_text())
-    assert tuple(module.ppy_collatz_collatz_sum(1, 1000)) == (0, g["sum_1_1000"])
+    assert tuple(module.collatz_collatz_sum(1, 1000)) == (0, g["sum_1_1000"])
