@@ -17,7 +17,15 @@ __all__ = ["module_source"]
 
 THREADS = 256
 #: Vectors each thread of a map kernel keeps in flight per loop trip.
-MAP_UNROLL = 2
+MAP_UNROLL = 1
+#: Resident 256-thread blocks per SM a vectorized map kernel is compiled for (full occupancy).
+MAP_MIN_BLOCKS = 0
+#: Resident blocks per SM a row kernel is compiled for (0: let the compiler choose).
+ROW_MIN_BLOCKS = 0
+#: Shared memory a pipelined row kernel may take per block (two row buffers per warp).
+ROW_SMEM_LIMIT = 100 * 1024
+#: Threads of a row kernel block when a row takes at most one warp.
+ROW_THREADS = 256
 
 _MATH32 = {"sqrt": "sqrtf", "sin": "sinf", "cos": "cosf", "tan": "tanf", "exp": "expf",
            "exp2": "exp2f", "log": "logf", "log2": "log2f", "log10": "log10f",
@@ -245,7 +253,7 @@ def _map_kernel(kernel: P.MapKernel, fn: P.TensorFunction, src: _Source) -> dict
         return {"elem": e, "rows": row, "cols": col, "scalar": "0"}[c]
 
     # --- scalar kernel (any rank; also the tail and unaligned fallback)
-    body_scalar.append(f"__global__ void __launch_bounds__({THREADS}) {name}_s("
+    body_scalar.append(f"static __global__ void __launch_bounds__({THREADS}) {name}_s("
                        + ", ".join(_kernel_params(kernel, extra)) + ") {")
     body_scalar.append("  (void)cols;")
     body_scalar.append("  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;"
@@ -304,7 +312,8 @@ def _map_kernel(kernel: P.MapKernel, fn: P.TensorFunction, src: _Source) -> dict
     vectorizable = not general and rank >= 1 and vec > 1
     if vectorizable:
         u = MAP_UNROLL
-        body_vec.append(f"__global__ void __launch_bounds__({THREADS}) {name}_v("
+        bounds = f"{THREADS}, {MAP_MIN_BLOCKS}" if MAP_MIN_BLOCKS else f"{THREADS}"
+        body_vec.append(f"static __global__ void __launch_bounds__({bounds}) {name}_v("
                         + ", ".join(_kernel_params(kernel, extra)) + ") {")
         body_vec.append(f"  constexpr int VEC = {vec};")
         body_vec.append("  const int64_t nvec = n / VEC; (void)cols;")
@@ -442,7 +451,7 @@ def _row_layout(kernel: P.RowKernel) -> dict:
         while -(-chunks // tpr) * vec > 32 and tpr < 1024:
             tpr *= 2
         nch = -(-chunks // tpr)
-    block = THREADS if tpr <= 32 else tpr
+    block = ROW_THREADS if tpr <= 32 else tpr
     return {"vec": vec, "chunks": chunks, "tpr": tpr, "nch": nch, "block": block,
             "rows_per_block": block // tpr if tpr <= 32 else 1}
 
@@ -509,34 +518,41 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
     name = kernel.name
     n_red = sum(1 for s in kernel.program if s.op == "reduce")
     warps = block // 32
-    L = []
-    L.append(f"__global__ void __launch_bounds__({block}) {name}("
-             + ", ".join(_kernel_params(kernel, extra)) + ") {")
+    masked = chunks % tpr != 0
+    elem_inputs = [i for i, c in enumerate(in_class) if c == "elem"]
+    # Pipelined form: persistent warps, each prefetching its next row group into shared
+    # memory (cp.async, double-buffered) while it computes the current one. It needs
+    # 16-byte chunks and a row group per warp (rows of at most 32 lanes).
+    pipelined = tpr <= 32 and elem_inputs and all(
+        vec * P.size_of(kernel.inputs[i].dtype) == 16 for i in elem_inputs)
+    rpw = 32 // tpr if tpr <= 32 else 1
+    seg = {}
+    buf_bytes = 0
+    for i in elem_inputs:
+        seg[i] = buf_bytes
+        buf_bytes += rpw * kernel.cols * P.size_of(kernel.inputs[i].dtype)
+        buf_bytes = (buf_bytes + 15) // 16 * 16
+    smem_bytes = warps * 2 * buf_bytes
+    if smem_bytes > ROW_SMEM_LIMIT:
+        pipelined = False
+    bounds = f"{block}, {ROW_MIN_BLOCKS}" if ROW_MIN_BLOCKS else f"{block}"
+    L = [f"static __global__ void __launch_bounds__({bounds}) {name}("
+         + ", ".join(_kernel_params(kernel, extra)) + ") {"]
     L.append(f"  constexpr int VEC = {vec}, TPR = {tpr}, NCH = {nch}, CHUNKS = {chunks}, "
              f"COLS = {kernel.cols};")
     L.append("  (void)CHUNKS; (void)status;")
     if tpr <= 32:
         L.append("  const int lane = threadIdx.x % TPR;")
-        L.append(f"  const int64_t slot = threadIdx.x / TPR; constexpr int64_t RPB = {block} / TPR;")
+        L.append(f"  const int64_t slot = (threadIdx.x & 31) / TPR; constexpr int64_t RPW = 32 / TPR;")
     else:
-        L.append("  const int lane = threadIdx.x; const int64_t slot = 0; constexpr int64_t RPB = 1;")
+        L.append("  const int lane = threadIdx.x; const int64_t slot = 0;")
         if n_red:
             L.append(f"  __shared__ float red_f[{max(n_red, 1)}][{warps}];")
             L.append(f"  __shared__ double red_d[{max(n_red, 1)}][{warps}];")
             L.append(f"  __shared__ int64_t red_i[{max(n_red, 1)}][{warps}];")
-    masked = chunks % tpr != 0
-    L.append("  // this lane's chunks of a row: chunk j*TPR + lane, VEC elements each")
-    # hoisted cols / scalar statements
     for i, operand in enumerate(kernel.inputs):
         ct = P.ctype(operand.dtype)
-        if in_class[i] == "cols":
-            L.append(f"  ppyb200::Vec<{ct}, VEC> c{i}[NCH];")
-            L.append("  #pragma unroll")
-            L.append("  for (int j = 0; j < NCH; ++j) {")
-            guard = "if (j * TPR + lane < CHUNKS) " if masked else ""
-            L.append(f"    {guard}c{i}[j] = ppyb200::load_vec_cached<{ct}, VEC>(in{i} + (int64_t)(j * TPR + lane) * VEC);")
-            L.append("  }")
-        elif in_class[i] == "scalar":
+        if in_class[i] == "scalar":
             L.append(f"  const {ct} s{i} = in{i}[0];")
 
     def value(var: str, where: str) -> str:
@@ -548,10 +564,16 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
     def input_expr(s: P.Stmt, where: str) -> str:
         i = s.args[0]
         c = in_class[i]
+        ct_i = P.ctype(kernel.inputs[i].dtype)
         if c == "elem":
-            e = f"x{i}[j].v[u]"
+            if pipelined:
+                e = (f"reinterpret_cast<const ppyb200::Vec<{ct_i}, VEC>*>(buf + {seg[i]} + "
+                     f"(int64_t)slot * COLS * {P.size_of(kernel.inputs[i].dtype)})[j * TPR + lane].v[u]")
+            else:
+                e = f"x{i}[j].v[u]"
         elif c == "cols":
-            e = f"c{i}[j].v[u]"
+            # per-column vectors (gamma, bias...) are read where they are used, from L1/L2
+            e = f"ppyb200::load_vec_cached<{ct_i}, VEC>(in{i} + (int64_t)(j * TPR + lane) * VEC).v[u]"
         elif c == "rows":
             e = f"r{i}"
         else:
@@ -560,132 +582,161 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
             e = f"ppyb200::convert<float, __nv_bfloat16>({e})"
         return e
 
-    # statements that are scalar or cols-only are hoisted out of the row loop
-    hoisted = [s for s in kernel.program if cls[s.var] in ("scalar", "cols")]
-    for s in hoisted:
+    # statements over scalars only are computed once per thread
+    for s in kernel.program:
+        if cls[s.var] != "scalar":
+            continue
         ct = P.ctype(_compute_dtype(s.dtype))
-        if cls[s.var] == "scalar":
-            if s.op == "input":
-                L.append(f"  const {ct} {s.var} = {input_expr(s, 'scalar')};")
-            else:
-                expr, pre = stmt_expr(s, lambda v: v, dtypes)
-                L.extend("  " + p for p in pre)
-                L.append(f"  const {ct} {s.var} = {expr};")
+        if s.op == "input":
+            L.append(f"  const {ct} {s.var} = {input_expr(s, 'scalar')};")
         else:
-            L.append(f"  {ct} {s.var}[NCH][VEC];")
-            L.append("  #pragma unroll")
-            L.append("  for (int j = 0; j < NCH; ++j) {")
-            L.append("    #pragma unroll")
-            L.append("    for (int u = 0; u < VEC; ++u) {")
-            if s.op == "input":
-                L.append(f"      {s.var}[j][u] = {input_expr(s, 'elem')};")
-            else:
-                expr, pre = stmt_expr(s, lambda v: value(v, "elem"), dtypes)
-                L.extend("      " + p for p in pre)
-                L.append(f"      {s.var}[j][u] = {expr};")
-            L.append("    }")
-            L.append("  }")
-    L.append("  const int64_t step = (int64_t)gridDim.x * RPB;")
-    L.append("  for (int64_t base = (int64_t)blockIdx.x * RPB; base < R; base += step) {")
-    L.append("    const int64_t row = base + slot;")
-    L.append("    const bool active = row < R;")
-    for i, operand in enumerate(kernel.inputs):
-        ct = P.ctype(operand.dtype)
-        if in_class[i] == "elem":
-            L.append(f"    ppyb200::Vec<{ct}, VEC> x{i}[NCH];")
-            L.append("    #pragma unroll")
-            L.append("    for (int j = 0; j < NCH; ++j) {")
+            expr, pre = stmt_expr(s, lambda v: v, dtypes)
+            L.extend("  " + p for p in pre)
+            L.append(f"  const {ct} {s.var} = {expr};")
+    # the body over one row (`row`, `active` and, when pipelined, `buf` in scope)
+    B = []
+    if not pipelined:
+        for i in elem_inputs:
+            ct = P.ctype(kernel.inputs[i].dtype)
+            B.append(f"ppyb200::Vec<{ct}, VEC> x{i}[NCH];")
+            B.append("#pragma unroll")
+            B.append("for (int j = 0; j < NCH; ++j) {")
             guard = "active && (j * TPR + lane < CHUNKS)" if masked else "active"
-            L.append(f"      if ({guard}) x{i}[j] = ppyb200::load_vec_stream<{ct}, VEC>("
+            B.append(f"  if ({guard}) x{i}[j] = ppyb200::load_vec_stream<{ct}, VEC>("
                      f"in{i} + row * COLS + (int64_t)(j * TPR + lane) * VEC);")
-            L.append(f"      else {{ for (int u = 0; u < VEC; ++u) x{i}[j].v[u] = {ct}{{}}; }}")
-            L.append("    }")
-        elif in_class[i] == "rows":
-            L.append(f"    const {ct} r{i} = active ? in{i}[row] : {ct}{{}};")
+            B.append(f"  else {{ for (int u = 0; u < VEC; ++u) x{i}[j].v[u] = {ct}{{}}; }}")
+            B.append("}")
+    for i, operand in enumerate(kernel.inputs):
+        if in_class[i] == "rows":
+            ct = P.ctype(operand.dtype)
+            B.append(f"const {ct} r{i} = active ? in{i}[row] : {ct}{{}};")
     red_index = 0
     for s in kernel.program:
         c = cls[s.var]
-        if c in ("scalar", "cols"):
+        if c == "scalar":
             continue
         ct = P.ctype(_compute_dtype(s.dtype))
         if s.op == "reduce":
             kind = s.attrs["kind"]
             arg = s.args[0]
             acc = f"{s.var}_acc"
-            L.append(f"    {ct} {acc} = {identity_literal(kind, _compute_dtype(s.dtype))};")
+            B.append(f"{ct} {acc} = {identity_literal(kind, _compute_dtype(s.dtype))};")
             if cls[arg] in ("elem", "cols"):
-                L.append("    #pragma unroll")
-                L.append("    for (int j = 0; j < NCH; ++j) {")
+                B.append("#pragma unroll")
+                B.append("for (int j = 0; j < NCH; ++j) {")
                 guard = "active && (j * TPR + lane < CHUNKS)" if masked else "active"
-                L.append(f"      if ({guard}) {{")
-                L.append("        #pragma unroll")
-                L.append("        for (int u = 0; u < VEC; ++u) "
+                B.append(f"  if ({guard}) {{")
+                B.append("    #pragma unroll")
+                B.append("    for (int u = 0; u < VEC; ++u) "
                          f"{acc} = {combine_expr(kind, acc, value(arg, 'elem'))};")
-                L.append("      }")
-                L.append("    }")
+                B.append("  }")
+                B.append("}")
             else:
-                # a fold over COLS copies of one value per row (e.g. a reduce of a row scalar)
-                L.append("    if (active) {")
-                L.append("      for (int j = 0; j < NCH; ++j) if (j * TPR + lane < CHUNKS) "
+                # a fold over COLS copies of one value per row (a reduce of a row scalar)
+                B.append("if (active) {")
+                B.append("  for (int j = 0; j < NCH; ++j) if (j * TPR + lane < CHUNKS) "
                          f"for (int u = 0; u < VEC; ++u) {acc} = {combine_expr(kind, acc, arg)};")
-                L.append("    }")
+                B.append("}")
             op = _COMBINE[kind]
             if tpr <= 32:
-                L.append(f"    const {ct} {s.var} = ppyb200::group_reduce<{op}, TPR>({acc});")
+                B.append(f"const {ct} {s.var} = ppyb200::group_reduce<{op}, TPR>({acc});")
             else:
                 smem = {"float": "red_f", "double": "red_d"}.get(ct, "red_i")
-                L.append(f"    {acc} = ppyb200::group_reduce<{op}, 32>({acc});")
-                L.append(f"    if ((threadIdx.x & 31) == 0) {smem}[{red_index}][threadIdx.x >> 5] = ({'float' if smem == 'red_f' else 'double' if smem == 'red_d' else 'int64_t'}){acc};")
-                L.append("    __syncthreads();")
-                L.append(f"    {ct} {s.var} = ({ct}){smem}[{red_index}][0];")
-                L.append(f"    for (int w = 1; w < {warps}; ++w) {s.var} = {combine_expr(kind, s.var, f'({ct}){smem}[{red_index}][w]')};")
+                smem_t = {"red_f": "float", "red_d": "double"}.get(smem, "int64_t")
+                B.append(f"{acc} = ppyb200::group_reduce<{op}, 32>({acc});")
+                B.append(f"if ((threadIdx.x & 31) == 0) {smem}[{red_index}][threadIdx.x >> 5] = ({smem_t}){acc};")
+                B.append("__syncthreads();")
+                B.append(f"{ct} {s.var} = ({ct}){smem}[{red_index}][0];")
+                B.append(f"for (int w = 1; w < {warps}; ++w) {s.var} = {combine_expr(kind, s.var, f'({ct}){smem}[{red_index}][w]')};")
             red_index += 1
             continue
         if c == "rows":
             if s.op == "input":
-                L.append(f"    const {ct} {s.var} = {input_expr(s, 'rows')};")
+                B.append(f"const {ct} {s.var} = {input_expr(s, 'rows')};")
             else:
                 expr, pre = stmt_expr(s, lambda v: v, dtypes)
-                L.extend("    " + p for p in pre)
-                L.append(f"    const {ct} {s.var} = {expr};")
+                B.extend(pre)
+                B.append(f"const {ct} {s.var} = {expr};")
             continue
-        # elem
-        L.append(f"    {ct} {s.var}[NCH][VEC];")
-        L.append("    #pragma unroll")
-        L.append("    for (int j = 0; j < NCH; ++j) {")
-        L.append("      #pragma unroll")
-        L.append("      for (int u = 0; u < VEC; ++u) {")
+        # elem and cols statements: one value per element of this lane's chunks
+        B.append(f"{ct} {s.var}[NCH][VEC];")
+        B.append("#pragma unroll")
+        B.append("for (int j = 0; j < NCH; ++j) {")
+        B.append("  #pragma unroll")
+        B.append("  for (int u = 0; u < VEC; ++u) {")
         if s.op == "input":
-            L.append(f"        {s.var}[j][u] = {input_expr(s, 'elem')};")
+            B.append(f"    {s.var}[j][u] = {input_expr(s, 'elem')};")
         else:
             expr, pre = stmt_expr(s, lambda v: value(v, "elem"), dtypes)
-            L.extend("        " + p for p in pre)
-            L.append(f"        {s.var}[j][u] = {expr};")
-        L.append("      }")
-        L.append("    }")
-    # stores
+            B.extend("    " + p for p in pre)
+            B.append(f"    {s.var}[j][u] = {expr};")
+        B.append("  }")
+        B.append("}")
     for j_out, (out, oc) in enumerate(zip(kernel.outputs, out_class)):
         ct = P.ctype(out.operand.dtype)
         src_ct = P.ctype(_compute_dtype(dtypes[out.var]))
         c = cls[out.var]
         if oc == "elem":
-            L.append("    if (active) {")
-            L.append("      #pragma unroll")
-            L.append("      for (int j = 0; j < NCH; ++j) {")
+            B.append("if (active) {")
+            B.append("  #pragma unroll")
+            B.append("  for (int j = 0; j < NCH; ++j) {")
             if masked:
-                L.append("        if (j * TPR + lane >= CHUNKS) continue;")
-            L.append(f"        ppyb200::Vec<{ct}, VEC> y;")
-            L.append("        #pragma unroll")
-            L.append(f"        for (int u = 0; u < VEC; ++u) y.v[u] = ppyb200::convert<{ct}, {src_ct}>({value(out.var, 'elem') if c in ('elem', 'cols') else out.var});")
-            L.append(f"        ppyb200::store_vec_stream<{ct}, VEC>(out{j_out} + row * COLS + (int64_t)(j * TPR + lane) * VEC, y);")
-            L.append("      }")
-            L.append("    }")
+                B.append("    if (j * TPR + lane >= CHUNKS) continue;")
+            B.append(f"    ppyb200::Vec<{ct}, VEC> y;")
+            B.append("    #pragma unroll")
+            B.append(f"    for (int u = 0; u < VEC; ++u) y.v[u] = ppyb200::convert<{ct}, {src_ct}>({value(out.var, 'elem') if c in ('elem', 'cols') else out.var});")
+            B.append(f"    ppyb200::store_vec_stream<{ct}, VEC>(out{j_out} + row * COLS + (int64_t)(j * TPR + lane) * VEC, y);")
+            B.append("  }")
+            B.append("}")
         else:
-            L.append(f"    if (active && lane == 0) out{j_out}[row] = ppyb200::convert<{ct}, {src_ct}>({out.var});")
-    if tpr > 32 and n_red:
-        L.append("    __syncthreads();")
-    L.append("  }")
-    L.append("}")
+            B.append(f"if (active && lane == 0) out{j_out}[row] = ppyb200::convert<{ct}, {src_ct}>({out.var});")
+    if pipelined:
+        L.append("  extern __shared__ __align__(16) unsigned char smem[];")
+        L.append(f"  constexpr int64_t WPB = {warps}, BUF = {buf_bytes};")
+        L.append("  const int64_t warp = threadIdx.x >> 5;")
+        L.append("  const int64_t groups = (R + RPW - 1) / RPW;")
+        L.append("  const int64_t first = (int64_t)blockIdx.x * WPB + warp;")
+        L.append("  const int64_t stride = (int64_t)gridDim.x * WPB;")
+        L.append("  unsigned char* wbuf = smem + warp * 2 * BUF;")
+        # prefetch of one row group into buffer b: every lane copies the chunks it reads
+        P_ = ["  auto prefetch = [&](int64_t g, int b) {",
+              "    const int64_t prow = g * RPW + slot;",
+              "    if (prow >= R) return;",
+              "    unsigned char* pb = wbuf + b * BUF;"]
+        for i in elem_inputs:
+            size = P.size_of(kernel.inputs[i].dtype)
+            P_.append("    #pragma unroll")
+            P_.append("    for (int j = 0; j < NCH; ++j) {")
+            if masked:
+                P_.append("      if (j * TPR + lane >= CHUNKS) continue;")
+            P_.append(f"      ppyb200::cp_async16(pb + {seg[i]} + (slot * COLS + (int64_t)(j * TPR + lane) * VEC) * {size}, "
+                      f"in{i} + prow * COLS + (int64_t)(j * TPR + lane) * VEC);")
+            P_.append("    }")
+        P_.append("  };")
+        L.extend(P_)
+        L.append("  if (first < groups) prefetch(first, 0);")
+        L.append("  ppyb200::cp_async_commit();")
+        L.append("  int b = 0;")
+        L.append("  for (int64_t g = first; g < groups; g += stride, b ^= 1) {")
+        L.append("    if (g + stride < groups) prefetch(g + stride, b ^ 1);")
+        L.append("    ppyb200::cp_async_commit();")
+        L.append("    ppyb200::cp_async_wait<1>();")
+        L.append("    const unsigned char* buf = wbuf + b * BUF;")
+        L.append("    const int64_t row = g * RPW + slot;")
+        L.append("    const bool active = row < R;")
+        L.extend("    " + line for line in B)
+        L.append("  }")
+        L.append("  ppyb200::cp_async_wait<0>();")
+        L.append("}")
+    else:
+        L.append("  {")
+        L.append(f"    constexpr int64_t RPB = {layout['rows_per_block']};")
+        L.append("    const int64_t row = (int64_t)blockIdx.x * RPB + (threadIdx.x / TPR);"
+                 if tpr <= 32 else "    const int64_t row = (int64_t)blockIdx.x;")
+        L.append("    const bool active = row < R;")
+        L.extend("    " + line for line in B)
+        L.append("  }")
+        L.append("}")
     src.kernels.append("\n".join(L))
     rows_count = P.spell_count(rows_shape)
     call_args = ", ".join([o.pointer for o in kernel.inputs] + [o.operand.pointer for o in kernel.outputs]
@@ -698,10 +749,24 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
     if align_checks and vec > 1:
         lines.append(f"    if (!({' && '.join(align_checks)})) {{ ppyb200_set_error(\"{name}: "
                      f"row operands must be {vec * 4}-byte aligned\"); return PPY_STATUS_RAISED; }}")
-    rpb = layout["rows_per_block"]
-    lines += [f"    const int64_t blocks = ppyb200_row_blocks(R, {rpb});",
-              f"    {name}<<<(unsigned)blocks, {block}, 0, stream>>>({call_args});",
-              "    launches++;", "  }", "}"]
+    if pipelined:
+        lines += [f"    static int resident = 0;  // blocks of {name} one SM holds",
+                  "    if (resident == 0) {",
+                  f"      cudaFuncSetAttribute({name}, cudaFuncAttributeMaxDynamicSharedMemorySize, {smem_bytes});",
+                  f"      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, {name}, {block}, {smem_bytes});",
+                  "      if (resident < 1) resident = 1;",
+                  "    }",
+                  f"    const int64_t groups = (R + {rpw} - 1) / {rpw};",
+                  f"    int64_t blocks = (groups + {warps} - 1) / {warps};",
+                  "    const int64_t cap = (int64_t)ppyb200_sm_count() * resident;",
+                  "    if (blocks > cap) blocks = cap;",
+                  f"    {name}<<<(unsigned)blocks, {block}, {smem_bytes}, stream>>>({call_args});",
+                  "    launches++;", "  }", "}"]
+    else:
+        rpb = layout["rows_per_block"]
+        lines += [f"    const int64_t blocks = (R + {rpb} - 1) / {rpb};",
+                  f"    {name}<<<(unsigned)blocks, {block}, 0, stream>>>({call_args});",
+                  "    launches++;", "  }", "}"]
     return {"launch": lines, "status": needs_status(kernel.program)}
 
 
@@ -721,7 +786,7 @@ def _reduce_all_kernel(kernel: P.ReduceAllKernel, fn: P.TensorFunction, src: _So
     extra = ["int64_t n"] + [f"{P.ctype(t)} p_{n}" for n, t in scalars] + [
         f"{acc_t}* __restrict__ partials", "int32_t* status"]
     params = [f"const {P.ctype(o.dtype)}* __restrict__ in{i}" for i, o in enumerate(kernel.inputs)]
-    L = [f"__global__ void __launch_bounds__({THREADS}) {name}_part(" + ", ".join(params + extra) + ") {",
+    L = [f"static __global__ void __launch_bounds__({THREADS}) {name}_part(" + ", ".join(params + extra) + ") {",
          f"  {acc_t} acc = {ident};", "  (void)status;"]
     L.append("  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; "
              "e += (int64_t)gridDim.x * blockDim.x) {")
@@ -757,7 +822,7 @@ def _reduce_all_kernel(kernel: P.ReduceAllKernel, fn: P.TensorFunction, src: _So
     L.append("  if (threadIdx.x == 0) partials[blockIdx.x] = acc;")
     L.append("}")
     out_ct = P.ctype(kernel.output.dtype)
-    L2 = [f"__global__ void __launch_bounds__({THREADS}) {name}_fin(const {acc_t}* __restrict__ partials, "
+    L2 = [f"static __global__ void __launch_bounds__({THREADS}) {name}_fin(const {acc_t}* __restrict__ partials, "
           f"int64_t parts, {out_ct}* __restrict__ out0) {{",
           f"  {acc_t} acc = {ident};",
           "  for (int64_t i = threadIdx.x; i < parts; i += blockDim.x) "
@@ -816,7 +881,7 @@ def _reduce_cols_kernel(kernel: P.ReduceColsKernel, fn: P.TensorFunction, src: _
     params = [f"const {P.ctype(o.dtype)}* __restrict__ in{i}" for i, o in enumerate(kernel.inputs)]
     extra = ["int64_t R", "int64_t C", "int64_t rows_per_chunk"] + [
         f"{P.ctype(t)} p_{n}" for n, t in scalars] + [f"{acc_t}* __restrict__ partials", "int32_t* status"]
-    L = [f"__global__ void __launch_bounds__({THREADS}) {name}_part(" + ", ".join(params + extra) + ") {",
+    L = [f"static __global__ void __launch_bounds__({THREADS}) {name}_part(" + ", ".join(params + extra) + ") {",
          "  (void)status;",
          "  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;",
          "  if (c >= C) return;",
@@ -842,7 +907,7 @@ def _reduce_cols_kernel(kernel: P.ReduceColsKernel, fn: P.TensorFunction, src: _
     L.append("  partials[(int64_t)blockIdx.y * C + c] = acc;")
     L.append("}")
     out_ct = P.ctype(kernel.output.dtype)
-    L2 = [f"__global__ void __launch_bounds__({THREADS}) {name}_fin(const {acc_t}* __restrict__ partials, "
+    L2 = [f"static __global__ void __launch_bounds__({THREADS}) {name}_fin(const {acc_t}* __restrict__ partials, "
           f"int64_t chunks, int64_t C, {out_ct}* __restrict__ out0) {{",
           "  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;",
           "  if (c >= C) return;",
@@ -976,7 +1041,7 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
         f"p_{p.name}" for p in scalars]
     result_line = f"  if (slot != nullptr) *slot = {fn.result_value};" if fn.result else ""
     # device ABI
-    D = [f'extern "C" int32_t {sym}__device({", ".join(_abi_params(fn.params) + ["int64_t* slot"])}) {{',
+    D = [f'extern "C" PPYB200_EXPORT int32_t {sym}__device({", ".join(_abi_params(fn.params) + ["int64_t* slot"])}) {{',
          "  ppyb200_bind_device();"]
     D += G
     for p in buffers:
@@ -989,7 +1054,7 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
     D.append("}")
     src.exports.append("\n".join(D))
     # host ABI
-    H = [f'extern "C" int32_t {sym}({", ".join(_abi_params(fn.params) + ["int64_t* slot"])}) {{',
+    H = [f'extern "C" PPYB200_EXPORT int32_t {sym}({", ".join(_abi_params(fn.params) + ["int64_t* slot"])}) {{',
          "  ppyb200_bind_device();"]
     H += G
     for p in buffers:
@@ -1035,7 +1100,7 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
         rt = P.ctype(k.result)
         op = _COMBINE[k.reduce]
         ident = identity_literal(k.reduce, k.result)
-        L = [f"__global__ void __launch_bounds__({T}) {k.name}_part("
+        L = [f"static __global__ void __launch_bounds__({T}) {k.name}_part("
              + ", ".join(caps + ["int64_t begin", "int64_t end", f"{rt} start",
                                  f"{rt}* __restrict__ partials", "int32_t* status"]) + ") {",
              f"  {rt} acc = start;",
@@ -1054,7 +1119,7 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
         L += _block_reduce_lines(rt, op, "acc")
         L.append("  if (threadIdx.x == 0) partials[blockIdx.x] = acc;")
         L.append("}")
-        L2 = [f"__global__ void __launch_bounds__({T}) {k.name}_fin(const {rt}* __restrict__ partials, "
+        L2 = [f"static __global__ void __launch_bounds__({T}) {k.name}_fin(const {rt}* __restrict__ partials, "
               f"int64_t parts, {rt} init, {rt}* __restrict__ out) {{",
               f"  {rt} acc = {ident};",
               f"  for (int64_t i = threadIdx.x; i < parts; i += blockDim.x) acc = {op}::apply(acc, partials[i]);"]
@@ -1088,7 +1153,7 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
         src.host.append("\n".join(H))
         return
     if k.kind == "for":
-        L = [f"__global__ void __launch_bounds__({T}) {k.name}_k("
+        L = [f"static __global__ void __launch_bounds__({T}) {k.name}_k("
              + ", ".join(caps + ["int64_t begin", "int64_t end", "int32_t* status"]) + ") {",
              "  const int64_t count = end - begin;",
              "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < count; "
@@ -1100,7 +1165,7 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
         extra_params, extra_args = [], []
     else:  # map
         ot = P.ctype(k.out_dtype)
-        L = [f"__global__ void __launch_bounds__({T}) {k.name}_k("
+        L = [f"static __global__ void __launch_bounds__({T}) {k.name}_k("
              + ", ".join(caps + ["int64_t begin", "int64_t end", f"{ot}* out", "int32_t* status"]) + ") {",
              "  const int64_t count = end - begin;",
              "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < count; "
@@ -1142,7 +1207,7 @@ def _scalar_function(fn: P.ScalarFunction, src: _Source) -> None:
             call.append(f"p_{p.name}")
     result_t = P.ctype(fn.result) if fn.result else None
     for suffix in ("", "__device"):
-        E = [f'extern "C" int32_t {fn.symbol}{suffix}({", ".join(atoms + ["int64_t* slot"])}) {{',
+        E = [f'extern "C" PPYB200_EXPORT int32_t {fn.symbol}{suffix}({", ".join(atoms + ["int64_t* slot"])}) {{',
              "  ppyb200_bind_device();"]
         if result_t:
             E.append(f"  {result_t} result{{}};")
@@ -1163,6 +1228,10 @@ PRELUDE = r'''// Generated by the PPy b200 backend from module @{module}. Do not
 #include <math.h>
 #include "ppyb200_device.cuh"
 #include "ppyb200.h"
+
+// Only the entry points leave the library: kernels and helpers have internal linkage,
+// so modules loaded side by side never call each other's code.
+#define PPYB200_EXPORT __attribute__((visibility("default")))
 
 // This library's CUDA runtime follows the device the calling thread bound with
 // ppyb200_init (each library carries its own runtime; the context is shared).

@@ -268,3 +268,24 @@ __device__ __forceinline__ void store_vec_stream(T* p, const Vec<T, VEC>& v) {
 }
 
 }  // namespace ppyb200
+
+namespace ppyb200 {
+
+// ---------------------------------------------------------------- async copies to shared
+
+// One 16-byte global->shared copy that completes asynchronously (cp.async, L2 only), and
+// the group fences around it: a row kernel prefetches its next row with these while it
+// computes the current one.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int PENDING>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(PENDING) : "memory");
+}
+
+}  // namespace ppyb200

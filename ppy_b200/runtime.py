@@ -211,7 +211,8 @@ class Module:
             toolchain.build_module(source, so)  # rebuilt only when stale
         if not so.exists():
             raise B200Error(f"{so} is missing and its source is not beside it")
-        self.lib = ctypes.CDLL(str(so), mode=ctypes.RTLD_GLOBAL)
+        # RTLD_LOCAL: a module's symbols stay its own (two builds may export one name)
+        self.lib = ctypes.CDLL(str(so), mode=ctypes.RTLD_LOCAL)
         self.device = _Namespace()
         self.functions: dict[str, Function] = {}
         for entry in self.manifest["functions"]:

@@ -47,6 +47,7 @@ def nvcc_version() -> str:
 
 def flags() -> list[str]:
     return [*GENCODE, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
+            "-diag-suppress", "177,550",
             "-Xcompiler", "-fPIC", "-shared", f"-I{CSRC}", f"-I{INCLUDE}"]
 
 
@@ -94,6 +95,7 @@ def build_module(source: Path, output: Path, force: bool = False) -> Path:
         return output
     runtime = build_runtime()
     compile_shared([source], output,
-                   [f"-L{runtime.parent}", "-lppyb200", f"-Xlinker=-rpath,{runtime.parent}"])
+                   ["-Xcompiler", "-fvisibility=hidden", f"-L{runtime.parent}", "-lppyb200",
+                    f"-Xlinker=-rpath,{runtime.parent}", "-Xlinker=-Bsymbolic"])
     stamp.write_text(digest)
     return output
