@@ -51,7 +51,7 @@ def _args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--workload", default="gelu", choices=["gelu", "rows", "collatz"])
+    p.add_argument("--workload", default="gelu", choices=["gelu", "rows", "collatz", "gemm"])
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU-baseline sample length (seconds of host work)")
@@ -355,10 +355,86 @@ class Collatz(Workload):
         return 0.0
 
 
-WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz}
+class Gemm(Workload):
+    metric = "matmul TFLOP/s: C = A @ B + bias, bf16 A/B, f32 accumulate and C, 8192^3"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    kernel = "matmul_bf16_kernel"
+    M = N = K = 8192
+    flops = 2 * 8192 ** 3
+
+    def inputs(self):
+        import torch
+
+        g = torch.Generator().manual_seed(0 + self.dist.rank)
+        k = self.K
+        self.a = (torch.randn(self.M, k, generator=g) / k ** 0.5).to(torch.bfloat16)
+        self.b = (torch.randn(k, self.N, generator=g) / k ** 0.5).to(torch.bfloat16)
+        self.bias = 0.02 * torch.randn(self.N, generator=g)
+
+    def config(self):
+        return {"workload": "matmul_bias_bf16", "m": self.M, "n": self.N, "k": self.K,
+                "seed": 0, "flops_per_step": self.flops,
+                "path": "tensor.matmul of tensor.convert(bf16) + bias through the built module: "
+                        "B [K,N] transposed to K-major, then the tcgen05 kernel",
+                "l2": "operands 256 MB > L2, no flush"}
+
+    def setup_device(self, runtime, torch):
+        self.module = runtime.load(PREBUILT / "matmul_bf16_8192" / "matmul_bf16_8192.json")
+        self.da, self.db, self.dbias = self.a.cuda(), self.b.cuda(), self.bias.cuda()
+        self.out = torch.empty(self.M, self.N, device="cuda")
+        self.pa, self.pb = self.a.pin_memory(), self.b.pin_memory()
+        self.pbias = self.bias.pin_memory()
+        self.pout = torch.empty(self.M, self.N).pin_memory()
+        self.dbt = self.db.t().contiguous()
+        import ctypes
+
+        self.lib = runtime.library()
+        self.lib.ppyb200_matmul_bf16_kmajor.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+
+    def step_device(self):
+        return self.module.device.matmul_bias_bf16(self.da, self.db, self.dbias, self.out).status
+
+    def step_host(self):
+        import torch
+
+        return self.module.matmul_bias_bf16(self.pa.view(torch.int16), self.pb.view(torch.int16),
+                                            self.pbias, self.pout).status
+
+    def kernel_step(self):
+        """The tcgen05 kernel alone (B already K-major): the roofline's launch."""
+        return self.lib.ppyb200_matmul_bf16_kmajor(self.da.data_ptr(), self.dbt.data_ptr(),
+                                                   self.dbias.data_ptr(), self.out.data_ptr(),
+                                                   self.M, self.N, self.K)
+
+    def h2d_d2h(self):
+        return 2 * 2 * self.M * self.K + 4 * self.N, 4 * self.M * self.N
+
+    def cpu_step(self, threads: int, oracle):
+        # NumPy f32 BLAS on the bf16-rounded values (the CPython reference of the path),
+        # over a bounded sample: the first 512 rows of A
+        rows = 512
+        a = self.a[:rows].float().numpy()
+        b = self.b.float().numpy()
+        _ = a @ b + self.bias.numpy()
+        return 2 * rows * self.N * self.K
+
+    def check(self, oracle):
+        import torch
+
+        rows = torch.tensor([0, 4095, 8191])
+        ref = self.a[rows].double() @ self.b.double() + self.bias.double()
+        got = self.out[rows.cuda()].cpu().double()
+        scale = torch.maximum(ref.abs(), ref.pow(2).mean().sqrt())
+        return float(((got - ref).abs() / scale).max())
+
+
+WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz, "gemm": Gemm}
 
 
 def units_per_step(w: Workload) -> float:
+    if isinstance(w, Gemm):
+        return float(w.flops)
     if isinstance(w, Collatz):
         if w.total_steps is None:
             w.total_steps = w.sum
@@ -369,6 +445,8 @@ def units_per_step(w: Workload) -> float:
 def to_metric(w: Workload, units: float, seconds: float) -> float:
     if w.unit == "GB/s":
         return units / seconds / 1e9
+    if w.unit == "TFLOP/s":
+        return units / seconds / 1e12
     return units / seconds
 
 
@@ -385,7 +463,8 @@ def cpu_baseline(w: Workload, seconds: float) -> dict:
         elapsed = time.perf_counter() - start
         if elapsed >= seconds:
             break
-    sample = {"gelu": "first 2^22 elements of the batch, repeated",
+    sample = {"gemm": "NumPy f32 BLAS on the first 512 rows of A, repeated",
+              "gelu": "first 2^22 elements of the batch, repeated",
               "rows": "first 4096 rows of the batch, repeated",
               "collatz": "starts [lo, lo + 2^22) of the range, repeated"}[
         next(k for k, v in WORKLOADS.items() if isinstance(w, v))]
@@ -447,27 +526,40 @@ def run_b200(args, dist: Dist) -> None:
         assert w.step_device() == 0
         assert w.step_host() == 0
     torch.cuda.synchronize()
-    # device-resident timing: one event pair around every step
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # device-resident timing: K steps back to back between one event pair
+    start_event = torch.cuda.Event(enable_timing=True)
+    end_event = torch.cuda.Event(enable_timing=True)
     launches0 = runtime.launches()
     dist.barrier()
     torch.cuda.synchronize()
     begin = time.perf_counter()
-    for i in range(args.steps):
-        starts[i].record(stream)
+    start_event.record(stream)
+    for _ in range(args.steps):
         status = w.step_device()
-        ends[i].record(stream)
         if status != 0:
             raise SystemExit(f"step failed with status {status}")
+    end_event.record(stream)
     torch.cuda.synchronize()
     dist.barrier()
     end = time.perf_counter()
     clocks.mark(begin, end)
     launches = runtime.launches() - launches0
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = starts[0].elapsed_time(ends[-1])
-    total_ms = dist.max(total_ms)
+    total_ms = dist.max(start_event.elapsed_time(end_event))
+    # the dominant kernel's own launch duration (for the workloads whose step is more than
+    # that one launch, timed alone over the same number of launches)
+    if hasattr(w, "kernel_step"):
+        k0 = torch.cuda.Event(enable_timing=True)
+        k1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        k0.record(stream)
+        for _ in range(args.steps):
+            if w.kernel_step() != 0:
+                raise SystemExit("kernel step failed")
+        k1.record(stream)
+        torch.cuda.synchronize()
+        step_ms = [k0.elapsed_time(k1) / args.steps]
+    else:
+        step_ms = [total_ms / args.steps]
     units = units_per_step(w)
     units_all = units * (dist.world if w.scaling == "weak" else 1)
     if isinstance(w, Collatz):
@@ -506,7 +598,15 @@ def run_b200(args, dist: Dist) -> None:
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": int(launches), "clocks": clock_info,
                 "max_rel_error_vs_oracle": error}
-        if w.unit == "GB/s":
+        if w.unit == "TFLOP/s":
+            pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] if (
+                REPO / "MEASURED_PEAKS.json").exists() else 1590.0
+            achieved = w.flops / (kernel_ms / 1e3) / 1e12
+            line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk_t,
+                                "unit": "TFLOP/s", "frac": achieved / pk_t,
+                                "traffic": traffic(w.kernel), "peak_source": pk["source"],
+                                "kernel": w.kernel, "kernel_ms": kernel_ms}
+        elif w.unit == "GB/s":
             achieved = w.bytes_per_step / (kernel_ms / 1e3) / 1e9
             line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
                                 "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],

@@ -106,6 +106,28 @@ int32_t ppyb200_check(int32_t cuda_error, const char *what);
 uint64_t ppyb200_launches(void);
 void ppyb200_count_launches(uint64_t count);
 
+/* ---------------------------------------------------------------- matmul */
+
+/* C[M,N] = A[M,K] @ B[K,N] (+ bias[N]): bf16 A and B, row-major; f32 bias (NULL for none);
+ * f32 accumulation and f32 C. Replaces LowerTensor.op_matmul, the naive i-j-k loop nest
+ * of ir/transforms/lower_tensor.py:756-776, for `tensor.matmul` / `linalg.matmul`
+ * (ir/dialects/tensor.py:475-488, linalg.py:309-320) of `tensor.convert`ed bf16 operands,
+ * with the `tensor.add` of a broadcast bias row FuseTensor leaves after it. Whole
+ * 128x256x64 tiles (M % 128, N % 256, K % 64) with a 16-byte aligned A run on tcgen05
+ * tensor cores (B is first transposed into the scratch arena); other shapes run on the
+ * CUDA cores. Device pointers; enqueued on the current stream. */
+int32_t ppyb200_matmul_bf16(const uint16_t *a, const uint16_t *b, const float *bias, float *c,
+                            int64_t m, int64_t n, int64_t k);
+
+/* ppyb200_matmul_bf16 with B given K-major, as bt[N,K] (the layout torch.nn.Linear keeps
+ * its weight in): tensor cores only; PPYB200_FALLBACK, with nothing launched, for shapes
+ * that are not whole tiles or operands not 16-byte aligned. */
+int32_t ppyb200_matmul_bf16_kmajor(const uint16_t *a, const uint16_t *bt, const float *bias,
+                                   float *c, int64_t m, int64_t n, int64_t k);
+
+/* bt[n*K + k] = b[k*N + n]: a bf16 [K,N] matrix into [N,K] (tiled through shared memory). */
+int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

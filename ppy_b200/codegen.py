@@ -1313,6 +1313,8 @@ def module_source(plan: P.ModulePlan, device_sources: list[str], kernels: list) 
     for fn in scalar_fns:
         _scalar_function(fn, src)
     parts = [PRELUDE.replace("{module}", plan.name)]
+    if any(k.kind == "matmul" for fn in plan.functions if fn.kind == "tensor" for k in fn.kernels):
+        parts.append('#include "gemm_sm100.cuh"\n#include "gemm_simt.cuh"')
     parts += prototypes
     parts += device_sources
     parts += src.kernels

@@ -1,0 +1,403 @@
+// Dense matmul on Blackwell tensor cores: D[M,N] (f32) = A[M,K] @ Bt[N,K]^T, then an
+// elementwise epilogue, for bf16 A and Bt (both K-major, i.e. row-major A and a row-major
+// [N,K] B^T -- the layout torch.nn.Linear keeps its weight in).
+//
+// One persistent CTA per SM walks the output tiles (128 x 256) in L2-friendly bands:
+//   warp 0   one thread issues TMA loads of A and Bt tiles (K-step 64, 128-byte swizzle)
+//            into a STAGES-deep shared-memory ring;
+//   warp 1   one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator
+//            and commits each stage back to the loader; it also owns the TMEM allocation;
+//   warps 2-5 read the accumulator out of TMEM (tcgen05.ld, one 32-lane quarter each),
+//            apply the epilogue and store rows of C coalesced through shared memory.
+// The accumulator is double-buffered (2 x 256 TMEM columns), so the epilogue of one tile
+// runs while the MMAs of the next are issued.
+//
+// Every mbarrier wait is bounded: past its limit the waiting thread records
+// PPYB200_DEVICE_RAISED in the call's status word and raises the CTA's abort flag; every
+// role then leaves its loop, the loader waits (bounded) for the copies it issued, the MMA
+// thread waits (bounded) for its MMAs, and the TMEM is freed before the CTA exits.
+// No load uses cluster multicast (the kernel may run on several GPUs of one node).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "ppyb200_device.cuh"
+
+namespace ppyb200 {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes: one swizzle row
+constexpr int UMMA_K = 16;
+constexpr int STAGES = 4;
+constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int ACC_COLS = BN;        // f32 accumulator columns per buffer
+constexpr int TMEM_COLS = 2 * ACC_COLS;
+constexpr int EPI_PITCH = 33;       // floats per staged row (32 + 1 pad: no bank conflicts)
+constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
+constexpr int GROUP_M = 16;         // tiles walk bands of 16 M-blocks for L2 reuse
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+
+// bf16 x bf16 -> f32, M = 128, N = 256, both operands K-major (PTX ISA, tcgen05
+// instruction descriptor: c_format bits 4-5, a/b format bits 7-12, N>>3 at bit 17,
+// M>>4 at bit 24).
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+struct Shared {
+  // the operand ring, 1024-byte aligned for the 128-byte swizzle
+  alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
+  float epi[EPI_WARPS][32][EPI_PITCH];
+  alignas(8) uint64_t full[STAGES];
+  alignas(8) uint64_t empty[STAGES];
+  alignas(8) uint64_t acc_full[2];
+  alignas(8) uint64_t acc_empty[2];
+  alignas(8) uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for the phase of `parity` to complete, at most WAIT_LIMIT tries; on giving up (or
+// when another role already gave up) raise the abort flag and the status word.
+__device__ __forceinline__ bool mbar_wait(Shared& s, uint64_t* bar, uint32_t parity,
+                                          int32_t* status) {
+  for (uint32_t tries = 0; tries < WAIT_LIMIT; ++tries) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*(volatile int*)&s.abort) return false;
+  }
+  *(volatile int*)&s.abort = 1;
+  if (status != nullptr) atomicMax(status, PPYB200_DEVICE_RAISED);
+  return false;
+}
+
+// A bounded wait used while tearing down: it ignores the abort flag.
+__device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t tries = 0; tries < WAIT_LIMIT; ++tries)
+    if (mbar_try_wait(bar, parity)) return;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile with the 128-byte swizzle: start
+// address (>>4) at bit 0, leading offset 16 B (unused for this layout) at bit 16, 1024 B
+// between 8-row groups at bit 32, descriptor version 1 at bit 46, swizzle mode 2 at bit 61.
+__device__ __forceinline__ uint64_t smem_desc(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tile_coords(int64_t t, int64_t m_blocks, int64_t n_blocks,
+                                            int64_t& mb, int64_t& nb) {
+  const int64_t per_group = (int64_t)GROUP_M * n_blocks;
+  const int64_t group = t / per_group;
+  const int64_t first_m = group * GROUP_M;
+  const int64_t rows = (m_blocks - first_m) < GROUP_M ? (m_blocks - first_m) : GROUP_M;
+  const int64_t r = t % per_group;
+  mb = first_m + r % rows;
+  nb = r / rows;
+}
+
+// The epilogue applied to every accumulator element: out = Epi(acc, row, col). It must
+// provide `__device__ float operator()(float acc, int64_t row, int64_t col) const`.
+struct BiasEpilogue {
+  const float* bias;
+  __device__ __forceinline__ float operator()(float acc, int64_t, int64_t col) const {
+    return bias != nullptr ? acc + __ldg(bias + col) : acc;
+  }
+};
+
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, float* __restrict__ c,
+                       int64_t m, int64_t n, int64_t k, Epi epi, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  Shared& s = *reinterpret_cast<Shared*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t m_blocks = m / BM, n_blocks = n / BN, k_blocks = k / BK;
+  const int64_t tiles = m_blocks * n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], EPI_WARPS);
+    }
+    mbar_init(&s.drain, 1);
+    s.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- loader
+      uint64_t it = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int64_t mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int st = (int)(it % STAGES);
+          const uint32_t phase = (uint32_t)((it / STAGES) & 1);
+          if (!mbar_wait(s, &s.empty[st], phase ^ 1, status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&s.full[st], STAGE_BYTES);
+          tma_load_2d(s.stage[st], &map_a, &s.full[st], (int32_t)(kb * BK), (int32_t)(mb * BM));
+          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], (int32_t)(kb * BK),
+                      (int32_t)(nb * BN));
+        }
+      }
+      // the copies this thread issued land before the CTA may leave
+      const uint64_t first = it > (uint64_t)STAGES ? it - STAGES : 0;
+      for (uint64_t j = first; j < it; ++j)
+        mbar_drain_wait(&s.full[j % STAGES], (uint32_t)((j / STAGES) & 1));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      uint64_t it = 0, acc_it = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++acc_it) {
+        const int a = (int)(acc_it & 1);
+        const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+        if (!mbar_wait(s, &s.acc_empty[a], aphase ^ 1, status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(a * ACC_COLS);
+        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int st = (int)(it % STAGES);
+          const uint32_t phase = (uint32_t)((it / STAGES) & 1);
+          if (!mbar_wait(s, &s.full[st], phase, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = smem_desc(s.stage[st]);
+          const uint64_t bdesc = smem_desc(s.stage[st] + A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            // advancing K by 16 bf16 = 32 bytes inside the swizzle row: +2 in addr >> 4
+            mma_bf16(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&s.empty[st]);
+        }
+        if (ok) mma_commit(&s.acc_full[a]);
+      }
+      // every MMA issued has finished before the accumulator memory is freed
+      mma_commit(&s.drain);
+      mbar_drain_wait(&s.drain, 0);
+    }
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32)
+    const int quarter = warp & 3;
+    const int ew = warp - 2;
+    float(*stage_rows)[EPI_PITCH] = s.epi[ew];
+    uint64_t acc_it = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_it) {
+      const int a = (int)(acc_it & 1);
+      const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+      if (!mbar_wait(s, &s.acc_full[a], aphase, status)) break;
+      tc_fence_after();
+      int64_t mb, nb;
+      tile_coords(t, m_blocks, n_blocks, mb, nb);
+      const int64_t row0 = mb * BM + quarter * 32;
+      const int64_t col0 = nb * BN;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS + chunk * 32),
+                  r);
+        // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
+        // memory so each store writes 32 consecutive floats of one row
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
+        __syncwarp();
+        const int64_t col = col0 + chunk * 32 + lane;
+#pragma unroll 4
+        for (int rr = 0; rr < 32; ++rr) {
+          const int64_t row = row0 + rr;
+          __stcs(c + row * n + col, epi(stage_rows[rr][lane], row, col));
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[a]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ---- host side
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiled encode_tiled() {
+  static EncodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* entry = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &entry, cudaEnableDefault, &found) ==
+            cudaSuccess &&
+        found == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(entry);
+  }
+  return fn;
+}
+
+// A row-major [rows, k] bf16 matrix as a TMA map of [box_rows, 64] tiles, 128-byte swizzle.
+inline bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+  EncodeTiled encode = encode_tiled();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool tileable(int64_t m, int64_t n, int64_t k) {
+  return m > 0 && n > 0 && k > 0 && m % BM == 0 && n % BN == 0 && k % BK == 0 &&
+         m / BM < (1ll << 31) && k < (1ll << 31) && m < (1ll << 31) && n < (1ll << 31);
+}
+
+inline size_t shared_bytes() { return sizeof(Shared) + 1024; }
+
+// Launch on `stream`; returns a cudaError_t (cudaErrorInvalidValue when the maps cannot be
+// made). The caller checks `tileable` and 16-byte alignment of a, bt first.
+template <class Epi>
+inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, float* c, int64_t m,
+                          int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
+                          cudaStream_t stream) {
+  CUtensorMap map_a, map_b;
+  if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN))
+    return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(matmul_bf16_kernel<Epi>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)shared_bytes());
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int64_t tiles = (m / BM) * (n / BN);
+  const int grid = (int)(tiles < sm_count ? tiles : sm_count);
+  matmul_bf16_kernel<Epi><<<grid, THREADS, shared_bytes(), stream>>>(map_a, map_b, c, m, n, k,
+                                                                     epi, status);
+  return cudaGetLastError();
+}
+
+}  // namespace gemm
+}  // namespace ppyb200

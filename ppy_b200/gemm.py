@@ -1,0 +1,113 @@
+"""Matmul kernels of a plan: `tensor.matmul` / `linalg.matmul` with the elementwise group
+that follows it (the bias add FuseTensor leaves) fused into the epilogue.
+
+bf16 operands in whole 128x256x64 tiles run on the tcgen05 kernel (csrc/gemm_sm100.cuh)
+after B, row-major [K, N] as the IR has it, is transposed into the scratch arena; every
+other case runs on the CUDA-core kernel (csrc/gemm_simt.cuh). The epilogue is a functor
+generated from the group's element program: input 0 is the product's element, the other
+inputs are read per row, per column, per element or once.
+"""
+
+from __future__ import annotations
+
+from . import plan as P
+from .codegen import _compute_dtype, _scalar_params, presence, stmt_expr
+from .scalar_c import Unsupported
+
+__all__ = ["matmul_launch"]
+
+
+def _classes(kernel: P.MatmulKernel) -> list[str]:
+    frame = (kernel.m, kernel.n)
+    out = []
+    for i, operand in enumerate(kernel.inputs):
+        if i == 0:
+            out.append("acc")
+            continue
+        flags = presence(operand.shape, frame)
+        out.append({(True, True): "elem", (True, False): "rows", (False, True): "cols",
+                    (False, False): "scalar"}[tuple(flags)])
+    return out
+
+
+def matmul_launch(kernel: P.MatmulKernel, fn: P.TensorFunction, src) -> dict:
+    params_by_name = {p.name: p for p in fn.params}
+    if len(kernel.outputs) != 1:
+        raise Unsupported("a matmul whose product and epilogue are both stored",
+                          "one stored result per matmul")
+    out = kernel.outputs[0]
+    if out.operand.dtype != "f32":
+        raise Unsupported(f"a matmul stored as {out.operand.dtype}", "f32 matmul results")
+    classes = _classes(kernel)
+    dtypes = {s.var: s.dtype for s in kernel.program}
+    scalars = _scalar_params(kernel.program, params_by_name)
+    name = kernel.name
+    # --- epilogue functor
+    members = []
+    for i, operand in enumerate(kernel.inputs[1:], start=1):
+        members.append(f"const {P.ctype(operand.dtype)}* __restrict__ in{i};")
+    members += [f"{P.ctype(t)} p_{n};" for n, t in scalars]
+    body = []
+    for s in kernel.program:
+        ct = P.ctype(_compute_dtype(s.dtype))
+        if s.op == "input":
+            i = s.args[0]
+            c = classes[i]
+            if c == "acc":
+                e = "acc"
+            else:
+                idx = {"elem": "row * n + col", "rows": "row", "cols": "col", "scalar": "0"}[c]
+                e = f"__ldg(in{i} + {idx})"
+                if kernel.inputs[i].dtype == "bf16":
+                    e = f"ppyb200::convert<float, __nv_bfloat16>({e})"
+            body.append(f"    const {ct} {s.var} = {e};")
+            continue
+        expr, pre = stmt_expr(s, lambda v: v, dtypes)
+        body.extend("    " + p for p in pre)
+        body.append(f"    const {ct} {s.var} = {expr};")
+    result_ct = P.ctype(_compute_dtype(dtypes[out.var]))
+    functor = [f"struct {name}_epi {{"] + ["  " + m for m in members] + [
+        "  int64_t n;",
+        "  int32_t* status;",
+        "  __device__ __forceinline__ float operator()(float acc, int64_t row, int64_t col) const {",
+        "    (void)row; (void)col;"] + body + [
+        f"    return ppyb200::convert<float, {result_ct}>({out.var});", "  }", "};"]
+    src.kernels.append("\n".join(functor))
+    # --- launch
+    a, b = kernel.a, kernel.b
+    m_expr = P.spell_count((kernel.m,))
+    init = ", ".join([o.pointer for o in kernel.inputs[1:]] + [f"p_{n}" for n, _ in scalars]
+                     + ["n", "status"])
+    ct = P.ctype(a.dtype)
+    lines = ["{",
+             f"  const int64_t m = {m_expr}, n = {kernel.n}, k = {kernel.k};",
+             f"  {name}_epi epi{{{init}}};",
+             f"  float* c = {out.operand.pointer};",
+             "  if (m > 0) {"]
+    tensor_cores = a.dtype == "bf16" and kernel.n % 256 == 0 and kernel.k % 64 == 0
+    if tensor_cores:
+        lines += [
+            f"    if (m % 128 == 0 && ppyb200_aligned({a.pointer}, 16)) {{",
+            "      // B is row-major [K, N]; the tensor-core kernel reads it K-major [N, K]",
+            "      __nv_bfloat16* bt = (__nv_bfloat16*)ppyb200_scratch_take(&scratch, n * k * 2);",
+            "      if (bt == nullptr) return PPY_STATUS_RAISED;",
+            f"      cudaError_t e = ppyb200::launch_transpose((const __nv_bfloat16*){b.pointer}, bt, k, n, stream);",
+            "      if (e == cudaSuccess) e = ppyb200::gemm::launch("
+            f"(const __nv_bfloat16*){a.pointer}, bt, c, m, n, k, epi, status, ppyb200_sm_count(), stream);",
+            f"      if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
+            "      launches += 2;",
+            "    } else {",
+            f"      cudaError_t e = ppyb200::simt::launch(({'const ' + ct}*){a.pointer}, ({'const ' + ct}*){b.pointer}, c, m, n, k, epi, stream);",
+            f"      if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
+            "      launches += 1;",
+            "    }"]
+    else:
+        lines += [
+            f"    cudaError_t e = ppyb200::simt::launch(({'const ' + ct}*){a.pointer}, ({'const ' + ct}*){b.pointer}, c, m, n, k, epi, stream);",
+            f"    if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
+            "    launches += 1;"]
+    lines += ["  }", "}"]
+    info = {"launch": lines, "status": tensor_cores, "gemm": True}
+    if tensor_cores:
+        info["scratch"] = f"ppyb200_round256((int64_t){kernel.n} * {kernel.k} * 2)"
+    return info

@@ -17,7 +17,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
 GOLDEN = REPO / "tests" / "golden"
-MODULES = ("gelu", "rows", "chain", "reductions", "collatz")
+MODULES = ("gelu", "rows", "chain", "reductions", "collatz", "matmul", "matmul_bf16",
+           "matmul_bf16_8192")
 
 
 def regenerate(names=MODULES, compile_library: bool = False) -> list[Path]:

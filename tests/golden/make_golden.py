@@ -415,8 +415,12 @@ def golden_matmul() -> None:
     status, _ = call(engine, "matmul_bias", a.ravel(), b.ravel(), bias, out.ravel())
     np.savez_compressed(HERE / "matmul.npz", a=a, b=b, bias=bias, out=out,
                         status=np.int32(status))
-    # The bf16 module: its IR only (the reference refuses to lower it).
+    # The bf16 modules: their IR only (the reference refuses to lower bf16 tensors).
     write_ppyir(shared_passes(build_matmul_bf16(), False), "matmul_bf16")
+    # the benchmark shape: C = A @ B + bias with M = N = K = 8192 (M bound at run time)
+    module = build_matmul_bf16(k=8192, n=8192)
+    module.name = "matmul_bf16_8192"
+    write_ppyir(shared_passes(module, False), "matmul_bf16_8192")
 
 
 COLLATZ = '''

@@ -1,0 +1,176 @@
+"""The matmul entry points through the C ABI, against a float64 evaluation of the same
+bf16 inputs (NumPy has no bf16; torch rounds them). Tolerance for the bf16 paths: the
+north star's 2e-2 relative on outputs, written here as |C - ref| <= 2e-2 * max(|ref|,
+rms(ref)); the tensor-core kernel accumulates in f32 and lands far inside it."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from ppy_b200 import runtime
+
+    if not torch.cuda.is_available():
+        pytest.fail("a GPU test ran without a CUDA device")
+    runtime.init(0)
+    runtime.set_stream(torch.cuda.current_stream())
+    lib = runtime.library()
+    for name in ("ppyb200_matmul_bf16", "ppyb200_matmul_bf16_kmajor"):
+        getattr(lib, name).argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+        getattr(lib, name).restype = ctypes.c_int32
+    lib.ppyb200_transpose_bf16.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                           ctypes.c_int64]
+    return lib
+
+
+def _operands(m, n, k, seed=0, bias=True):
+    g = torch.Generator().manual_seed(seed)
+    a = (torch.randn(m, k, generator=g) / k ** 0.5).to(torch.bfloat16)
+    b = (torch.randn(k, n, generator=g) / k ** 0.5).to(torch.bfloat16)
+    c = (0.02 * torch.randn(n, generator=g)) if bias else None
+    return a, b, c
+
+
+def _reference(a, b, bias):
+    ref = a.double() @ b.double()
+    if bias is not None:
+        ref = ref + bias.double()
+    return ref.numpy()
+
+
+def _check(out, ref, rel=2e-2):
+    out = out.cpu().double().numpy()
+    scale = np.maximum(np.abs(ref), np.sqrt(np.mean(ref ** 2)))
+    err = np.abs(out - ref) / scale
+    assert float(err.max()) <= rel, float(err.max())
+    return float(err.max())
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 192), (1024, 1024, 1024),
+                                   (384, 768, 768)])
+def test_tensor_core_matmul_matches_float64(lib, m, n, k):
+    a, b, bias = _operands(m, n, k)
+    da, db, dbias = a.cuda(), b.cuda(), bias.cuda()
+    out = torch.full((m, n), float("nan"), device="cuda")
+    status = lib.ppyb200_matmul_bf16(_ptr(da), _ptr(db), _ptr(dbias), _ptr(out), m, n, k)
+    torch.cuda.synchronize()
+    assert status == 0
+    err = _check(out, _reference(a, b, bias))
+    assert err < 1e-4  # f32 accumulation of bf16 products: far inside the bound
+
+
+def test_kmajor_entry_and_no_bias(lib):
+    m, n, k = 256, 256, 128
+    a, b, _ = _operands(m, n, k, seed=1, bias=False)
+    da, bt = a.cuda(), b.t().contiguous().cuda()  # held: a pointer alone keeps nothing alive
+    out = torch.empty((m, n), device="cuda")
+    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(da), _ptr(bt), None, _ptr(out), m, n, k) == 0
+    torch.cuda.synchronize()
+    _check(out, _reference(a, b, None), rel=1e-4)
+
+
+def test_kmajor_refuses_ragged_shapes(lib):
+    a = torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda")
+    bt = torch.zeros(256, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(100, 256, device="cuda")
+    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(a), _ptr(bt), None, _ptr(out), 100, 256, 64) == 1
+
+
+@pytest.mark.parametrize("m,n,k", [(100, 70, 33), (1, 256, 64), (129, 257, 65)])
+def test_ragged_shapes_run_on_cuda_cores(lib, m, n, k):
+    a, b, bias = _operands(m, n, k, seed=2)
+    da, db, dbias = a.cuda(), b.cuda(), bias.cuda()
+    out = torch.empty((m, n), device="cuda")
+    status = lib.ppyb200_matmul_bf16(_ptr(da), _ptr(db), _ptr(dbias), _ptr(out), m, n, k)
+    torch.cuda.synchronize()
+    assert status == 0
+    _check(out, _reference(a, b, bias), rel=1e-4)
+
+
+def test_transpose(lib):
+    b = torch.randn(300, 70).to(torch.bfloat16).cuda()
+    bt = torch.empty(70, 300, dtype=torch.bfloat16, device="cuda")
+    assert lib.ppyb200_transpose_bf16(_ptr(b), _ptr(bt), 300, 70) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(bt, b.t())
+
+
+def test_bench_size_matmul_properties(lib):
+    """8192^3 (the benchmark shape): spot rows against float64, and linearity in B."""
+    m = n = k = 8192
+    a, b, bias = _operands(m, n, k, seed=3)
+    da, db, dbias = a.cuda(), b.cuda(), bias.cuda()
+    out = torch.empty((m, n), device="cuda")
+    assert lib.ppyb200_matmul_bf16(_ptr(da), _ptr(db), _ptr(dbias), _ptr(out), m, n, k) == 0
+    torch.cuda.synchronize()
+    rows = torch.tensor([0, 1, 127, 128, 4095, 8191])
+    ref = (a[rows].double() @ b.double() + bias.double()).numpy()
+    _check(out[rows.cuda()], ref, rel=1e-4)
+    # linearity: A @ (2B) is exactly 2 (A @ B) (scaling by 2 is exact in bf16 and f32)
+    plain = torch.empty_like(out)
+    twice = torch.empty_like(out)
+    db2 = db * 2
+    assert lib.ppyb200_matmul_bf16(_ptr(da), _ptr(db), None, _ptr(plain), m, n, k) == 0
+    assert lib.ppyb200_matmul_bf16(_ptr(da), _ptr(db2), None, _ptr(twice), m, n, k) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(twice, 2 * plain)
+
+
+# ---------------------------------------------------------------- through built modules
+
+
+def _module(name):
+    from conftest import PREBUILT
+    from ppy_b200 import runtime
+
+    return runtime.load(PREBUILT / name / f"{name}.json")
+
+
+def test_f32_matmul_module_matches_the_reference(lib):
+    """matmul.ppyir (f32, 64x96 @ 96x80 + bias) against PPy's LLVM JIT output."""
+    from conftest import GOLDEN, within
+
+    d = np.load(GOLDEN / "matmul.npz")
+    module = _module("matmul")
+    out = np.zeros_like(d["out"])
+    status, _ = module.matmul_bias(d["a"].ravel(), d["b"].ravel(), d["bias"], out.ravel())
+    assert status == int(d["status"]) == 0
+    within(out, d["out"])
+
+
+@pytest.mark.parametrize("m", [256, 100, 0])
+def test_bf16_matmul_module(lib, m):
+    """matmul_bf16.ppyir: whole tiles on tensor cores, other row counts on CUDA cores."""
+    module = _module("matmul_bf16")
+    a, b, bias = _operands(max(m, 1), 256, 128, seed=4)
+    a = a[:m]
+    out = np.zeros((m, 256), np.float32)
+    status, _ = module.matmul_bias_bf16(a.view(torch.int16).numpy().view(np.uint16).ravel(),
+                                        b.view(torch.int16).numpy().view(np.uint16).ravel(),
+                                        bias.numpy(), out.ravel())
+    assert status == 0
+    if m:
+        _check(torch.from_numpy(out), _reference(a, b, bias), rel=1e-4)
+
+
+def test_bench_shape_module_rows(lib):
+    module = _module("matmul_bf16_8192")
+    a, b, bias = _operands(128, 8192, 8192, seed=5)
+    da, db, dbias = a.cuda(), b.cuda(), bias.cuda()
+    out = torch.empty((128, 8192), device="cuda")
+    assert module.device.matmul_bias_bf16(da, db, dbias, out).status == 0
+    torch.cuda.synchronize()
+    _check(out, _reference(a, b, bias), rel=1e-4)
