@@ -128,6 +128,24 @@ int32_t ppyb200_matmul_bf16_kmajor(const uint16_t *a, const uint16_t *bt, const 
 /* bt[n*K + k] = b[k*N + n]: a bf16 [K,N] matrix into [N,K] (tiled through shared memory). */
 int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64_t n);
 
+/* ---------------------------------------------------------------- without allocation */
+
+/* Floats in the fixed device array ppyb200_colmax_abs_f32_noalloc keeps its partials in. */
+#define PPYB200_NOALLOC_PARTIALS 262144
+
+/* out[c] = max over r of |x[r*cols + c]| (NaN-propagating, -inf for no rows): the
+ * leading-axis reduction the backend builds for tensor.reduce(abs(x), axes=(0,), op="max"),
+ * for callers that cannot allocate device memory at call time (memory reserved once at
+ * start-up, or owned by another framework's allocator). It has no counterpart in the
+ * reference: it exists for those callers. It allocates nothing -- its partial results live
+ * in a static 1 MiB __device__ array (PPYB200_NOALLOC_PARTIALS floats) that every GPU
+ * loading this library holds until exit -- and refuses rows wider than
+ * PPYB200_NOALLOC_PARTIALS columns with PPYB200_RAISED. Its first call on a device looks
+ * up the array's address (cudaGetSymbolAddress): make that call before any stream
+ * capture. All calls share the array; calls that overlap on the GPU race on it. Device
+ * pointers; enqueued on the current stream. */
+int32_t ppyb200_colmax_abs_f32_noalloc(const float *x, int64_t rows, int64_t cols, float *out);
+
 #ifdef __cplusplus
 }
 #endif
