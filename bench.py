@@ -51,7 +51,8 @@ def _args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--workload", default="gelu", choices=["gelu", "rows", "collatz", "gemm"])
+    p.add_argument("--workload", default="gelu",
+                   choices=["gelu", "rows", "collatz", "gemm", "gpt2"])
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU-baseline sample length (seconds of host work)")
@@ -429,12 +430,121 @@ class Gemm(Workload):
         return float(((got - ref).abs() / scale).max())
 
 
-WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz, "gemm": Gemm}
+class Gpt2(Workload):
+    metric = "GPT-2-124M forward tokens/s: batch 32 x 1024, logits out"
+    unit = "tokens/s"
+    dtype = "bf16"
+    kernel = "gpt2_forward"
+    scaling = "strong"
+    BATCH, LENGTH = 32, 1024
+
+    def inputs(self):
+        import torch
+
+        world, rank = self.dist.world, self.dist.rank
+        if self.BATCH % world:
+            raise SystemExit("the batch of 32 does not split over this many GPUs")
+        per = self.BATCH // world
+        g = torch.Generator().manual_seed(0)
+        ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
+        self.ids = ids[rank * per:(rank + 1) * per].contiguous()
+
+    def config(self):
+        return {"workload": "gpt2_124m_forward", "batch": self.BATCH, "seq_len": self.LENGTH,
+                "layers": 12, "width": 768, "heads": 12, "vocab": 50257,
+                "parallelism": f"dp{self.dist.world}", "weights": "N(0, 0.02) seed 0, bf16",
+                "l2": "weights 250 MB + activations > L2, no flush"}
+
+    def setup_device(self, runtime, torch):
+        from ppy_b200 import gpt2
+
+        self.model = gpt2.GPT2(gpt2.GPT2_124M, seed=0)
+        self.gpt2 = gpt2
+        self.dids = self.ids.cuda()
+        self.pids = self.ids.pin_memory()
+        b = self.ids.shape[0]
+        self.logits = torch.empty(b, self.LENGTH, 50257, device="cuda")
+        self.last = torch.empty(b, 50257).pin_memory()
+
+    def step_device(self):
+        self.model.forward(self.dids, self.logits)
+        return 0
+
+    def step_host(self):
+        # e2e: ids from pinned host memory in, the last position's logits out (what the
+        # next-token step reads)
+        self.dids.copy_(self.pids, non_blocking=True)
+        self.model.forward(self.dids, self.logits)
+        self.last.copy_(self.logits[:, -1], non_blocking=True)
+        return 0
+
+    def h2d_d2h(self):
+        b = self.ids.shape[0]
+        return 8 * b * self.LENGTH, 4 * b * 50257
+
+    def cpu_step(self, threads: int, oracle):
+        # the reference's GPT-2 path is torch ATen: its CPU forward, one sequence of 1024,
+        # f32 weights (the bf16-rounded values)
+        import torch
+
+        if not hasattr(self, "cpu_model"):
+            self.cpu_model = _cpu_reference_model()
+        torch.set_num_threads(threads)
+        with torch.no_grad():
+            self.cpu_model(self.ids[:1])
+        return float(self.LENGTH)
+
+    def check(self, oracle):
+        import torch
+
+        ids = self.dids[:1, :256]
+        got = self.model.forward(ids)
+        ref = self.model.reference_forward(ids)
+        torch.cuda.synchronize()
+        return float((got - ref).abs().max() / ref.abs().max())
+
+
+def _cpu_reference_model():
+    """The GPT-2 forward of examples/46_gpt2/gpt2.ppy:18-57 (torch ATen ops) on the CPU, the
+    same shapes and init, f32."""
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(0)
+    c, v, layers, heads = 768, 50257, 12, 12
+
+    def normal(*shape):
+        return (0.02 * torch.randn(*shape, generator=g)).to(torch.bfloat16).float()
+
+    wte, wpe = normal(v, c), normal(1024, c)
+    blocks = [(normal(3 * c, c), normal(c, c), normal(4 * c, c), normal(c, 4 * c))
+              for _ in range(layers)]
+    ones, zeros = torch.ones(c), torch.zeros(c)
+
+    def forward(ids):
+        b, n = ids.shape
+        x = wte[ids] + wpe[:n]
+        for wqkv, wo, wfc, wproj in blocks:
+            h = F.layer_norm(x, (c,), ones, zeros, 1e-5)
+            q, k, vv = F.linear(h, wqkv).split(c, dim=-1)
+            shape = lambda t: t.reshape(b, n, heads, c // heads).transpose(1, 2)  # noqa: E731
+            a = F.scaled_dot_product_attention(shape(q), shape(k), shape(vv), is_causal=True)
+            x = x + F.linear(a.transpose(1, 2).reshape(b, n, c), wo)
+            f = F.gelu(F.linear(F.layer_norm(x, (c,), ones, zeros, 1e-5), wfc), approximate="tanh")
+            x = x + F.linear(f, wproj)
+        return F.layer_norm(x, (c,), ones, zeros, 1e-5) @ wte.t()
+
+    return forward
+
+
+WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz, "gemm": Gemm, "gpt2": Gpt2}
 
 
 def units_per_step(w: Workload) -> float:
     if isinstance(w, Gemm):
         return float(w.flops)
+    if isinstance(w, Gpt2):
+        return float(w.ids.numel())
     if isinstance(w, Collatz):
         if w.total_steps is None:
             w.total_steps = w.sum
@@ -463,7 +573,8 @@ def cpu_baseline(w: Workload, seconds: float) -> dict:
         elapsed = time.perf_counter() - start
         if elapsed >= seconds:
             break
-    sample = {"gemm": "NumPy f32 BLAS on the first 512 rows of A, repeated",
+    sample = {"gpt2": "torch CPU forward (f32) of the first sequence (1 x 1024), repeated",
+              "gemm": "NumPy f32 BLAS on the first 512 rows of A, repeated",
               "gelu": "first 2^22 elements of the batch, repeated",
               "rows": "first 4096 rows of the batch, repeated",
               "collatz": "starts [lo, lo + 2^22) of the range, repeated"}[
@@ -565,6 +676,8 @@ def run_b200(args, dist: Dist) -> None:
     if isinstance(w, Collatz):
         sums = dist.sum_i64([w.sum])
         units_all = float(sums[0])
+    if isinstance(w, Gpt2):
+        units_all = float(dist.sum_i64([int(units)])[0])
     value = to_metric(w, units_all * args.steps, total_ms / 1e3)
     kernel_ms = float(np.mean(step_ms))
     # end to end through the host-memory entry point (pinned host buffers)
@@ -612,6 +725,21 @@ def run_b200(args, dist: Dist) -> None:
                                 "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                                 "traffic": traffic(w.kernel), "peak_source": pk["source"],
                                 "kernel": w.kernel, "kernel_ms": kernel_ms}
+        elif isinstance(w, Gpt2):
+            pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (
+                REPO / "MEASURED_PEAKS.json").exists() else 1400.0
+            table = w.model.profile(w.dids, w.logits)
+            name, (count, ms, flops) = max(table.items(), key=lambda kv: kv[1][1])
+            achieved = flops / (ms / 1e3) / 1e12
+            forward_tflops = w.gpt2.sequence_flops(w.gpt2.GPT2_124M, w.ids.shape[0],
+                                                   w.LENGTH) / (total_ms / args.steps / 1e3) / 1e12
+            line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk_t,
+                                "unit": "TFLOP/s", "frac": achieved / pk_t, "traffic": None,
+                                "peak_source": "measured (sustained)", "kernel": name,
+                                "kernel_ms": ms / count,
+                                "forward_tflops": forward_tflops,
+                                "forward_frac": forward_tflops / pk_t,
+                                "breakdown_ms": {k: round(v[1], 3) for k, v in table.items()}}
         else:
             line["roofline"] = {"bound": "int-issue", "achieved": value, "peak": None,
                                 "unit": w.unit, "frac": None, "traffic": None,

@@ -128,6 +128,36 @@ int32_t ppyb200_matmul_bf16_kmajor(const uint16_t *a, const uint16_t *bt, const 
 /* bt[n*K + k] = b[k*N + n]: a bf16 [K,N] matrix into [N,K] (tiled through shared memory). */
 int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64_t n);
 
+/* ---------------------------------------------------------------- GPT-2 pieces */
+
+/* x[t, c] = wte[ids[t], c] + wpe[t % length, c] (bf16 tables, f32 x [tokens, width]): the
+ * embedding of examples/46_gpt2/gpt2.ppy:212 (`wte[ids] + wpe[0:length]`). An id outside
+ * [0, vocab) reads nothing and raises `*status` (may be NULL) to 2. width % 8 == 0. */
+int32_t ppyb200_gpt2_embed(const int64_t *ids, const uint16_t *wte, const uint16_t *wpe,
+                           float *x, int64_t tokens, int64_t length, int64_t width,
+                           int64_t vocab, int32_t *status);
+
+/* out[M,N] (bf16) = act(a[M,K] @ w[N,K]^T + bias[N]), act 0 = identity, 1 = GELU-tanh, on
+ * tcgen05 tensor cores: F.linear (+ F.gelu(approximate="tanh")) of gpt2.ppy:49-56 with the
+ * torch.nn.Linear weight layout. K % 64 == 0. `*status` (may be NULL) is raised to 2 if the
+ * kernel gives up a bounded wait. */
+int32_t ppyb200_linear_bf16(const uint16_t *a, const uint16_t *w, const float *bias,
+                            uint16_t *out, int64_t m, int64_t n, int64_t k, int32_t activation,
+                            int32_t *status);
+
+/* residual[M,N] (f32) += a[M,K] @ w[N,K]^T + bias[N]: `torch.add(x, F.linear(...))` of
+ * gpt2.ppy:54,57, the residual updated in place by the tensor-core epilogue. */
+int32_t ppyb200_linear_residual(const uint16_t *a, const uint16_t *w, const float *bias,
+                                float *residual, int64_t m, int64_t n, int64_t k,
+                                int32_t *status);
+
+/* Causal self-attention, F.scaled_dot_product_attention(q, k, v, is_causal=True) of
+ * gpt2.ppy:52: qkv is [batch*length, 3*heads*64] bf16 (q, k, v side by side, head h at
+ * columns h*64), out is [batch*length, heads*64] bf16 (heads merged, as gpt2.ppy:53).
+ * Scores and softmax in f32. head_dim 64, length % 128 == 0. */
+int32_t ppyb200_attention_causal_bf16(const uint16_t *qkv, uint16_t *out, int64_t batch,
+                                      int64_t length, int64_t heads, int64_t head_dim);
+
 /* ---------------------------------------------------------------- without allocation */
 
 /* Floats in the fixed device array ppyb200_colmax_abs_f32_noalloc keeps its partials in. */

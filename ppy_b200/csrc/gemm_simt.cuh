@@ -23,9 +23,8 @@ __device__ __forceinline__ float to_f32(T v) {
 // A 32x32 output tile per 32x8 block; every thread computes 4 outputs of one column.
 template <class T, class Epi>
 __global__ void __launch_bounds__(256) matmul_kernel(const T* __restrict__ a,
-                                                     const T* __restrict__ b,
-                                                     float* __restrict__ c, int64_t m, int64_t n,
-                                                     int64_t k, Epi epi) {
+                                                     const T* __restrict__ b, int64_t m,
+                                                     int64_t n, int64_t k, Epi epi) {
   __shared__ float as[TILE][TILE + 1];
   __shared__ float bs[TILE][TILE + 1];
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -52,16 +51,16 @@ __global__ void __launch_bounds__(256) matmul_kernel(const T* __restrict__ a,
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t row = row0 + ty + 8 * i, col = col0 + tx;
-    if (row < m && col < n) c[row * n + col] = epi(acc[i], row, col);
+    if (row < m && col < n) epi.store(acc[i], row, col);
   }
 }
 
 template <class T, class Epi>
-inline cudaError_t launch(const T* a, const T* b, float* c, int64_t m, int64_t n, int64_t k,
-                          Epi epi, cudaStream_t stream) {
+inline cudaError_t launch(const T* a, const T* b, int64_t m, int64_t n, int64_t k, Epi epi,
+                          cudaStream_t stream) {
   if (m <= 0 || n <= 0) return cudaSuccess;
   dim3 grid((unsigned)((n + TILE - 1) / TILE), (unsigned)((m + TILE - 1) / TILE));
-  matmul_kernel<T, Epi><<<grid, dim3(32, 8), 0, stream>>>(a, b, c, m, n, k, epi);
+  matmul_kernel<T, Epi><<<grid, dim3(32, 8), 0, stream>>>(a, b, m, n, k, epi);
   return cudaGetLastError();
 }
 

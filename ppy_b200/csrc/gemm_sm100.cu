@@ -38,17 +38,17 @@ int32_t ppyb200_matmul_bf16_kmajor(const uint16_t* a, const uint16_t* bt, const 
   }
   if (m == 0 || n == 0) return PPYB200_OK;
   if (!ppyb200::gemm::tileable(m, n, k) || !aligned16(a) || !aligned16(bt)) {
-    ppyb200_set_error("ppyb200_matmul_bf16_kmajor: M % 128, N % 256, K % 64 and 16-byte "
-                      "aligned operands are required");
+    ppyb200_set_error("ppyb200_matmul_bf16_kmajor: K % 64 and 16-byte aligned operands are "
+                      "required");
     return PPYB200_FALLBACK;
   }
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(ppyb200_stream());
   int32_t* status = ppyb200_status_word();
   if (status == nullptr) return PPYB200_RAISED;
-  ppyb200::gemm::BiasEpilogue epi{bias};
+  ppyb200::gemm::BiasEpilogue epi{bias, c, n};
   cudaError_t e = ppyb200::gemm::launch(reinterpret_cast<const __nv_bfloat16*>(a),
-                                        reinterpret_cast<const __nv_bfloat16*>(bt), c, m, n, k,
-                                        epi, status, ppyb200_sm_count(), stream);
+                                        reinterpret_cast<const __nv_bfloat16*>(bt), m, n, k, epi,
+                                        status, ppyb200_sm_count(), stream);
   return finish(e, "ppyb200_matmul_bf16_kmajor", 1);
 }
 
@@ -63,8 +63,8 @@ int32_t ppyb200_matmul_bf16(const uint16_t* a, const uint16_t* b, const float* b
   const auto* A = reinterpret_cast<const __nv_bfloat16*>(a);
   const auto* B = reinterpret_cast<const __nv_bfloat16*>(b);
   if (!ppyb200::gemm::tileable(m, n, k) || !aligned16(a)) {
-    ppyb200::gemm::BiasEpilogue epi{bias};
-    cudaError_t e = ppyb200::simt::launch(A, B, c, m, n, k, epi, stream);
+    ppyb200::gemm::BiasEpilogue epi{bias, c, n};
+    cudaError_t e = ppyb200::simt::launch(A, B, m, n, k, epi, stream);
     return finish(e, "ppyb200_matmul_bf16 (CUDA cores)", 1);
   }
   // B arrives row-major [K, N]; the tensor-core kernel reads it K-major ([N, K]).

@@ -1,6 +1,8 @@
-// Dense matmul on Blackwell tensor cores: D[M,N] (f32) = A[M,K] @ Bt[N,K]^T, then an
-// elementwise epilogue, for bf16 A and Bt (both K-major, i.e. row-major A and a row-major
-// [N,K] B^T -- the layout torch.nn.Linear keeps its weight in).
+// Dense matmul on Blackwell tensor cores: D[M,N] = A[M,K] @ Bt[N,K]^T accumulated in f32,
+// then an elementwise epilogue that stores it, for bf16 A and Bt (both K-major: a row-major
+// A and a row-major [N,K] B^T -- the layout torch.nn.Linear keeps its weight in). K must be
+// a multiple of 64; M and N may be ragged (TMA fills the out-of-range part of an edge tile
+// with zeros and the epilogue skips it).
 //
 // One persistent CTA per SM walks the output tiles (128 x 256) in L2-friendly bands:
 //   warp 0   one thread issues TMA loads of A and Bt tiles (K-step 64, 128-byte swizzle)
@@ -180,26 +182,29 @@ __device__ __forceinline__ void tile_coords(int64_t t, int64_t m_blocks, int64_t
   nb = r / rows;
 }
 
-// The epilogue applied to every accumulator element: out = Epi(acc, row, col). It must
-// provide `__device__ float operator()(float acc, int64_t row, int64_t col) const`.
+// The epilogue: `__device__ void store(float acc, int64_t row, int64_t col) const` is called
+// once per element of C inside [0, M) x [0, N); consecutive lanes get consecutive columns of
+// one row, so stores through it coalesce. This one writes acc (+ bias[col]) as f32.
 struct BiasEpilogue {
   const float* bias;
-  __device__ __forceinline__ float operator()(float acc, int64_t, int64_t col) const {
-    return bias != nullptr ? acc + __ldg(bias + col) : acc;
+  float* c;
+  int64_t ldc;
+  __device__ __forceinline__ void store(float acc, int64_t row, int64_t col) const {
+    __stcs(c + row * ldc + col, bias != nullptr ? acc + __ldg(bias + col) : acc);
   }
 };
 
 template <class Epi>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
-                       const __grid_constant__ CUtensorMap map_b, float* __restrict__ c,
-                       int64_t m, int64_t n, int64_t k, Epi epi, int32_t* status) {
+                       const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
+                       int64_t k, Epi epi, int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   Shared& s = *reinterpret_cast<Shared*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t m_blocks = m / BM, n_blocks = n / BN, k_blocks = k / BK;
+  const int64_t m_blocks = (m + BM - 1) / BM, n_blocks = (n + BN - 1) / BN, k_blocks = k / BK;
   const int64_t tiles = m_blocks * n_blocks;
 
   if (threadIdx.x == 0) {
@@ -313,10 +318,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
         __syncwarp();
         const int64_t col = col0 + chunk * 32 + lane;
+        if (col < n) {
 #pragma unroll 4
-        for (int rr = 0; rr < 32; ++rr) {
-          const int64_t row = row0 + rr;
-          __stcs(c + row * n + col, epi(stage_rows[rr][lane], row, col));
+          for (int rr = 0; rr < 32; ++rr) {
+            const int64_t row = row0 + rr;
+            if (row < m) epi.store(stage_rows[rr][lane], row, col);
+          }
         }
         __syncwarp();
       }
@@ -368,9 +375,11 @@ inline bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// What the tensor-core kernel takes: K a whole number of 64-wide steps (the row stride of A
+// and Bt, K * 2 bytes, is then a multiple of 16 as TMA requires), extents within int32.
 inline bool tileable(int64_t m, int64_t n, int64_t k) {
-  return m > 0 && n > 0 && k > 0 && m % BM == 0 && n % BN == 0 && k % BK == 0 &&
-         m / BM < (1ll << 31) && k < (1ll << 31) && m < (1ll << 31) && n < (1ll << 31);
+  return m > 0 && n > 0 && k > 0 && k % BK == 0 && k < (1ll << 31) && m < (1ll << 31) &&
+         n < (1ll << 31);
 }
 
 inline size_t shared_bytes() { return sizeof(Shared) + 1024; }
@@ -378,8 +387,8 @@ inline size_t shared_bytes() { return sizeof(Shared) + 1024; }
 // Launch on `stream`; returns a cudaError_t (cudaErrorInvalidValue when the maps cannot be
 // made). The caller checks `tileable` and 16-byte alignment of a, bt first.
 template <class Epi>
-inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, float* c, int64_t m,
-                          int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
+inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m, int64_t n,
+                          int64_t k, Epi epi, int32_t* status, int sm_count,
                           cudaStream_t stream) {
   CUtensorMap map_a, map_b;
   if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN))
@@ -392,10 +401,10 @@ inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, float
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int64_t tiles = (m / BM) * (n / BN);
+  const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = (int)(tiles < sm_count ? tiles : sm_count);
-  matmul_bf16_kernel<Epi><<<grid, THREADS, shared_bytes(), stream>>>(map_a, map_b, c, m, n, k,
-                                                                     epi, status);
+  matmul_bf16_kernel<Epi><<<grid, THREADS, shared_bytes(), stream>>>(map_a, map_b, m, n, k, epi,
+                                                                     status);
   return cudaGetLastError();
 }
 

@@ -1,7 +1,7 @@
 """Matmul kernels of a plan: `tensor.matmul` / `linalg.matmul` with the elementwise group
 that follows it (the bias add FuseTensor leaves) fused into the epilogue.
 
-bf16 operands in whole 128x256x64 tiles run on the tcgen05 kernel (csrc/gemm_sm100.cuh)
+bf16 operands with K a multiple of 64 run on the tcgen05 kernel (csrc/gemm_sm100.cuh)
 after B, row-major [K, N] as the IR has it, is transposed into the scratch arena; every
 other case runs on the CUDA-core kernel (csrc/gemm_simt.cuh). The epilogue is a functor
 generated from the group's element program: input 0 is the product's element, the other
@@ -36,8 +36,8 @@ def matmul_launch(kernel: P.MatmulKernel, fn: P.TensorFunction, src) -> dict:
         raise Unsupported("a matmul whose product and epilogue are both stored",
                           "one stored result per matmul")
     out = kernel.outputs[0]
-    if out.operand.dtype != "f32":
-        raise Unsupported(f"a matmul stored as {out.operand.dtype}", "f32 matmul results")
+    if out.operand.dtype not in ("f32", "bf16", "f64"):
+        raise Unsupported(f"a matmul stored as {out.operand.dtype}", "float matmul results")
     classes = _classes(kernel)
     dtypes = {s.var: s.dtype for s in kernel.program}
     scalars = _scalar_params(kernel.program, params_by_name)
@@ -66,44 +66,46 @@ def matmul_launch(kernel: P.MatmulKernel, fn: P.TensorFunction, src) -> dict:
         body.extend("    " + p for p in pre)
         body.append(f"    const {ct} {s.var} = {expr};")
     result_ct = P.ctype(_compute_dtype(dtypes[out.var]))
+    out_ct = P.ctype(out.operand.dtype)
     functor = [f"struct {name}_epi {{"] + ["  " + m for m in members] + [
         "  int64_t n;",
         "  int32_t* status;",
-        "  __device__ __forceinline__ float operator()(float acc, int64_t row, int64_t col) const {",
-        "    (void)row; (void)col;"] + body + [
-        f"    return ppyb200::convert<float, {result_ct}>({out.var});", "  }", "};"]
+        f"  {out_ct}* __restrict__ out;",
+        "  __device__ __forceinline__ void store(float acc, int64_t row, int64_t col) const {"
+        ] + body + [
+        f"    out[row * n + col] = ppyb200::convert<{out_ct}, {result_ct}>({out.var});",
+        "  }", "};"]
     src.kernels.append("\n".join(functor))
     # --- launch
     a, b = kernel.a, kernel.b
     m_expr = P.spell_count((kernel.m,))
     init = ", ".join([o.pointer for o in kernel.inputs[1:]] + [f"p_{n}" for n, _ in scalars]
-                     + ["n", "status"])
+                     + ["n", "status", out.operand.pointer])
     ct = P.ctype(a.dtype)
     lines = ["{",
              f"  const int64_t m = {m_expr}, n = {kernel.n}, k = {kernel.k};",
              f"  {name}_epi epi{{{init}}};",
-             f"  float* c = {out.operand.pointer};",
              "  if (m > 0) {"]
-    tensor_cores = a.dtype == "bf16" and kernel.n % 256 == 0 and kernel.k % 64 == 0
+    tensor_cores = a.dtype == "bf16" and kernel.k % 64 == 0
     if tensor_cores:
         lines += [
-            f"    if (m % 128 == 0 && ppyb200_aligned({a.pointer}, 16)) {{",
+            f"    if (ppyb200_aligned({a.pointer}, 16) && m < (1ll << 31)) {{",
             "      // B is row-major [K, N]; the tensor-core kernel reads it K-major [N, K]",
             "      __nv_bfloat16* bt = (__nv_bfloat16*)ppyb200_scratch_take(&scratch, n * k * 2);",
             "      if (bt == nullptr) return PPY_STATUS_RAISED;",
             f"      cudaError_t e = ppyb200::launch_transpose((const __nv_bfloat16*){b.pointer}, bt, k, n, stream);",
             "      if (e == cudaSuccess) e = ppyb200::gemm::launch("
-            f"(const __nv_bfloat16*){a.pointer}, bt, c, m, n, k, epi, status, ppyb200_sm_count(), stream);",
+            f"(const __nv_bfloat16*){a.pointer}, bt, m, n, k, epi, status, ppyb200_sm_count(), stream);",
             f"      if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
             "      launches += 2;",
             "    } else {",
-            f"      cudaError_t e = ppyb200::simt::launch(({'const ' + ct}*){a.pointer}, ({'const ' + ct}*){b.pointer}, c, m, n, k, epi, stream);",
+            f"      cudaError_t e = ppyb200::simt::launch(({'const ' + ct}*){a.pointer}, ({'const ' + ct}*){b.pointer}, m, n, k, epi, stream);",
             f"      if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
             "      launches += 1;",
             "    }"]
     else:
         lines += [
-            f"    cudaError_t e = ppyb200::simt::launch(({'const ' + ct}*){a.pointer}, ({'const ' + ct}*){b.pointer}, c, m, n, k, epi, stream);",
+            f"    cudaError_t e = ppyb200::simt::launch(({'const ' + ct}*){a.pointer}, ({'const ' + ct}*){b.pointer}, m, n, k, epi, stream);",
             f"    if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
             "    launches += 1;"]
     lines += ["  }", "}"]

@@ -115,6 +115,41 @@ def build_rows(cols: int = 1024):
     return m
 
 
+def build_layernorm(cols: int = 768):
+    """GPT-2's layernorm as tensor IR: f32 rows in, bf16 rows out (the next matmul's A)."""
+    from ppy_compiler.ir import BF16, F32, I64, BufferType, Builder, IRModule
+    from ppy_compiler.ir import shape as shapes
+    from ppy_compiler.ir.dialects import core, tensor
+
+    r = shapes.Symbol("R")
+    m = IRModule("gpt2_layernorm")
+    m.require("tensor", 1)
+    mat = tensor.tensor_type(F32, (r, cols))
+    col = tensor.tensor_type(F32, (r, 1))
+    vec = tensor.tensor_type(F32, (cols,))
+    f = m.add_function("layernorm_bf16", [("x", BufferType(F32)), ("gamma", BufferType(F32)),
+                                          ("beta", BufferType(F32)), ("out", BufferType(BF16))],
+                       [I64])
+    b = Builder(f.add_entry_block())
+    xb, gb, bb, out = f.entry.arguments
+    x = tensor.load(b, xb, mat, "x")
+    g = tensor.load(b, gb, vec, "gamma")
+    be = tensor.load(b, bb, vec, "beta")
+    ew = lambda name, p, q: tensor.elementwise(b, name, p, q)  # noqa: E731
+
+    def k(v):
+        return tensor.fill(b, core.const(b, v, F32), col)
+
+    mean = ew("div", tensor.reduce(b, x, (1,), "add", keepdims=True), k(float(cols)))
+    d = ew("sub", x, mean)
+    var = ew("div", tensor.reduce(b, ew("mul", d, d), (1,), "add", keepdims=True), k(float(cols)))
+    rstd = ew("div", k(1.0), tensor.unary(b, "sqrt", ew("add", var, k(1e-5))))
+    y = ew("add", ew("mul", ew("mul", d, rstd), g), be)
+    tensor.store(b, tensor.convert(b, y, BF16), out)
+    core.ret(b, core.const(b, 0, I64))
+    return m
+
+
 def build_chain():
     """The reference's own fusion fixture (tests/test_tensor_fusion.py:133-163), f64."""
     from ppy_compiler.ir import F64, I64, BufferType, Builder, IRModule
@@ -519,6 +554,12 @@ def _with_collatz_max(text: str) -> str:
     return encode(module)
 
 
+def golden_layernorm() -> None:
+    """IR only: bf16 tensors are refused by the reference's LowerTensor; the parity of
+    this module is checked against torch.layer_norm on the GPU."""
+    write_ppyir(shared_passes(build_layernorm(), False), "gpt2_layernorm")
+
+
 def golden_collatz(reference: Path) -> None:
     from ppy_compiler.ir import decode
 
@@ -588,6 +629,7 @@ def main() -> None:
     golden_rows()
     golden_reductions()
     golden_matmul()
+    golden_layernorm()
     golden_collatz(options.reference)
     print("golden fixtures written to", HERE)
 

@@ -1,0 +1,168 @@
+"""GPT-2 pieces and the whole forward against torch float32 on the same bf16 weights (the
+reference's GPT-2 path is torch ATen, examples/46_gpt2/gpt2.ppy:18-57).
+
+Tolerances. Pieces: |y - ref| <= tol * max(|ref|, rms(ref)) per element. Logits (the north
+star's 2e-2 relative on logits for the bf16 GEMM paths), as relative errors of the tensor:
+max|y - ref| / max|ref| <= 2e-2 and ||y - ref|| / ||ref|| <= 2e-2. The forward rounds the
+matmul operands to bf16 (layernorm outputs, attention output, GELU output, P); the torch
+reference rounds nothing, so their difference is that rounding."""
+
+from __future__ import annotations
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+F = pytest.importorskip("torch.nn.functional")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from ppy_b200 import gpt2, runtime
+
+    if not torch.cuda.is_available():
+        pytest.fail("a GPU test ran without a CUDA device")
+    runtime.init(0)
+    runtime.set_stream(torch.cuda.current_stream())
+    lib = runtime.library()
+    gpt2._bind(lib)
+    return lib
+
+
+def _close(out, ref, rel=2e-2):
+    out, ref = out.double(), ref.double()
+    scale = torch.maximum(ref.abs(), ref.pow(2).mean().sqrt())
+    err = float(((out - ref).abs() / scale).max())
+    assert err <= rel, err
+    return err
+
+
+def _close_logits(out, ref, rel=2e-2):
+    out, ref = out.double(), ref.double()
+    diff = (out - ref)
+    worst = float(diff.abs().max() / ref.abs().max())
+    norm = float(diff.norm() / ref.norm())
+    assert worst <= rel and norm <= rel, (worst, norm)
+    return worst, norm
+
+
+def test_attention_matches_sdpa(lib):
+    batch, length, heads, d = 2, 256, 12, 64
+    width = heads * d
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qkv = torch.randn(batch * length, 3 * width, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(batch * length, width, device="cuda", dtype=torch.bfloat16)
+    assert lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), out.data_ptr(), batch, length,
+                                             heads, d) == 0
+    torch.cuda.synchronize()
+    q, k, v = qkv.float().split(width, dim=1)
+    shape = lambda t: t.reshape(batch, length, heads, d).transpose(1, 2)  # noqa: E731
+    ref = F.scaled_dot_product_attention(shape(q), shape(k), shape(v), is_causal=True)
+    ref = ref.transpose(1, 2).reshape(batch * length, width)
+    _close(out, ref)  # P and the output rounded to bf16: ~1e-2 at worst
+
+
+def test_attention_refuses_lengths_off_the_tile(lib):
+    qkv = torch.zeros(100, 3 * 768, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(100, 768, device="cuda", dtype=torch.bfloat16)
+    assert lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), out.data_ptr(), 1, 100, 12, 64) == -1
+
+
+def test_embed(lib):
+    vocab, width, length, batch = 1000, 768, 256, 2
+    g = torch.Generator(device="cuda").manual_seed(1)
+    wte = torch.randn(vocab, width, device="cuda", generator=g).to(torch.bfloat16)
+    wpe = torch.randn(1024, width, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.randint(0, vocab, (batch, length), device="cuda", generator=g)
+    x = torch.empty(batch * length, width, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert lib.ppyb200_gpt2_embed(ids.data_ptr(), wte.data_ptr(), wpe.data_ptr(), x.data_ptr(),
+                                  batch * length, length, width, vocab, status.data_ptr()) == 0
+    torch.cuda.synchronize()
+    ref = (wte.float()[ids] + wpe.float()[:length]).reshape(batch * length, width)
+    assert torch.equal(x, ref) and int(status.item()) == 0
+    # an id outside the table reads nothing and raises the status word
+    ids[0, 0] = vocab
+    assert lib.ppyb200_gpt2_embed(ids.data_ptr(), wte.data_ptr(), wpe.data_ptr(), x.data_ptr(),
+                                  batch * length, length, width, vocab, status.data_ptr()) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2
+
+
+@pytest.mark.parametrize("activation", [0, 1])
+def test_linear_bf16(lib, activation):
+    m, n, k = 512, 3072, 768
+    g = torch.Generator(device="cuda").manual_seed(2)
+    a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(torch.bfloat16)
+    b = 0.1 * torch.randn(n, device="cuda", generator=g)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    assert lib.ppyb200_linear_bf16(a.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(), m, n,
+                                   k, activation, None) == 0
+    torch.cuda.synchronize()
+    ref = F.linear(a.float(), w.float(), b)
+    if activation:
+        ref = F.gelu(ref, approximate="tanh")
+    _close(out, ref, rel=1e-2)  # bf16 output rounding
+
+
+def test_linear_residual(lib):
+    m, n, k = 256, 768, 3072
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(torch.bfloat16)
+    b = 0.1 * torch.randn(n, device="cuda", generator=g)
+    x = torch.randn(m, n, device="cuda", generator=g)
+    ref = x + F.linear(a.float(), w.float(), b)
+    assert lib.ppyb200_linear_residual(a.data_ptr(), w.data_ptr(), b.data_ptr(), x.data_ptr(), m,
+                                       n, k, None) == 0
+    torch.cuda.synchronize()
+    assert _close(x, ref) < 1e-4
+
+
+def test_layernorm_module_matches_torch(lib):
+    from conftest import PREBUILT
+    from ppy_b200 import runtime
+
+    module = runtime.load(PREBUILT / "gpt2_layernorm" / "gpt2_layernorm.json")
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = 3 * torch.randn(1000, 768, device="cuda", generator=g) + 1
+    gamma = 1 + 0.1 * torch.randn(768, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(768, device="cuda", generator=g)
+    out = torch.empty(1000, 768, device="cuda", dtype=torch.bfloat16)
+    assert module.device.layernorm_bf16(x, gamma, beta, out).status == 0
+    torch.cuda.synchronize()
+    ref = F.layer_norm(x, (768,), gamma, beta, 1e-5)
+    _close(out, ref, rel=1e-2)  # bf16 output rounding (2^-8 relative)
+
+
+def test_small_gpt2_forward_matches_torch(lib):
+    from ppy_b200.gpt2 import GPT2, Config
+
+    model = GPT2(Config(layers=2), seed=0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ids = torch.randint(0, 50257, (2, 256), device="cuda", generator=g)
+    logits = model.forward(ids)
+    torch.cuda.synchronize()
+    assert model.status() == 0
+    ref = model.reference_forward(ids)
+    _close_logits(logits, ref)
+
+
+def test_gpt2_124m_forward_matches_torch(lib):
+    from ppy_b200.gpt2 import GPT2, GPT2_124M
+
+    model = GPT2(GPT2_124M, seed=0)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    ids = torch.randint(0, 50257, (2, 1024), device="cuda", generator=g)
+    logits = model.forward(ids)
+    torch.cuda.synchronize()
+    assert model.status() == 0
+    ref = model.reference_forward(ids)
+    _close_logits(logits, ref)
+    # the same sequence alone gives the same logits (batch rows are independent)
+    first = logits[1].clone()
+    alone = model.forward(ids[1:2])
+    torch.cuda.synchronize()
+    assert torch.equal(alone[0], first)

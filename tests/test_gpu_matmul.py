@@ -82,11 +82,24 @@ def test_kmajor_entry_and_no_bias(lib):
     _check(out, _reference(a, b, None), rel=1e-4)
 
 
-def test_kmajor_refuses_ragged_shapes(lib):
-    a = torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda")
-    bt = torch.zeros(256, 64, dtype=torch.bfloat16, device="cuda")
-    out = torch.zeros(100, 256, device="cuda")
-    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(a), _ptr(bt), None, _ptr(out), 100, 256, 64) == 1
+def test_kmajor_refuses_k_not_a_multiple_of_64(lib):
+    a = torch.zeros(128, 96, dtype=torch.bfloat16, device="cuda")
+    bt = torch.zeros(256, 96, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(128, 256, device="cuda")
+    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(a), _ptr(bt), None, _ptr(out), 128, 256, 96) == 1
+
+
+@pytest.mark.parametrize("m,n,k", [(100, 70, 64), (1, 50257, 128), (300, 520, 192)])
+def test_tensor_cores_take_ragged_m_and_n(lib, m, n, k):
+    """Edge tiles: TMA zero-fills past M and N, the epilogue stores only inside."""
+    a, b, bias = _operands(m, n, k, seed=6)
+    da, dbt, dbias = a.cuda(), b.t().contiguous().cuda(), bias.cuda()
+    out = torch.full((m + 1, n), 7.0, device="cuda")  # one row past C must stay untouched
+    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(da), _ptr(dbt), _ptr(dbias), _ptr(out), m, n,
+                                          k) == 0
+    torch.cuda.synchronize()
+    _check(out[:m], _reference(a, b, bias), rel=1e-4)
+    assert torch.all(out[m] == 7.0)
 
 
 @pytest.mark.parametrize("m,n,k", [(100, 70, 33), (1, 256, 64), (129, 257, 65)])
