@@ -9,8 +9,9 @@
 //            into a STAGES-deep shared-memory ring;
 //   warp 1   one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator
 //            and commits each stage back to the loader; it also owns the TMEM allocation;
-//   warps 2-5 read the accumulator out of TMEM (tcgen05.ld, one 32-lane quarter each),
-//            apply the epilogue and store rows of C coalesced through shared memory.
+//   warps 2-9 read the accumulator out of TMEM (tcgen05.ld; warp w reads lane quarter w % 4,
+//            two warps per quarter split the columns), apply the epilogue and store rows
+//            of C coalesced through shared memory.
 // The accumulator is double-buffered (2 x 256 TMEM columns), so the epilogue of one tile
 // runs while the MMAs of the next are issued.
 //
@@ -36,8 +37,8 @@ constexpr int BN = 256;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes: one swizzle row
 constexpr int UMMA_K = 16;
 constexpr int STAGES = 4;
-constexpr int THREADS = 192;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -185,12 +186,30 @@ __device__ __forceinline__ void tile_coords(int64_t t, int64_t m_blocks, int64_t
 // The epilogue: `__device__ void store(float acc, int64_t row, int64_t col) const` is called
 // once per element of C inside [0, M) x [0, N); consecutive lanes get consecutive columns of
 // one row, so stores through it coalesce. This one writes acc (+ bias[col]) as f32.
+//
+// The kernel hands an epilogue 32 rows of one column at a time:
+// `store_column(const float (&acc)[32], int64_t row0, int64_t col, int64_t rows)` stores
+// acc[r] at (row0 + r, col) for r < rows. `for_column` gives that from a per-element store.
+// (Every loop over the 32 values is unrolled in full: an index the compiler cannot resolve
+// would put the array in local memory.)
+template <class Epi>
+__device__ __forceinline__ void for_column(const Epi& epi, const float (&acc)[32], int64_t row0,
+                                           int64_t col, int64_t rows) {
+#pragma unroll
+  for (int r = 0; r < 32; ++r)
+    if (r < rows) epi.store(acc[r], row0 + r, col);
+}
+
 struct BiasEpilogue {
   const float* bias;
   float* c;
   int64_t ldc;
   __device__ __forceinline__ void store(float acc, int64_t row, int64_t col) const {
     __stcs(c + row * ldc + col, bias != nullptr ? acc + __ldg(bias + col) : acc);
+  }
+  __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, int64_t col,
+                                               int64_t rows) const {
+    for_column(*this, acc, row0, col, rows);
   }
 };
 
@@ -293,9 +312,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_drain_wait(&s.drain, 0);
     }
   } else {
-    // ---- epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32)
+    // ---- epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32); the two warps of a
+    // quarter take alternate halves of the 256 columns
     const int quarter = warp & 3;
     const int ew = warp - 2;
+    const int half = ew >> 2;
     float(*stage_rows)[EPI_PITCH] = s.epi[ew];
     uint64_t acc_it = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_it) {
@@ -307,23 +328,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       tile_coords(t, m_blocks, n_blocks, mb, nb);
       const int64_t row0 = mb * BM + quarter * 32;
       const int64_t col0 = nb * BN;
+      const int64_t rows = m - row0 < 32 ? m - row0 : 32;
 #pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      for (int c4 = 0; c4 < BN / 64; ++c4) {
+        const int chunk = half * (BN / 64) + c4;
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS + chunk * 32),
                   r);
         // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
-        // memory so each store writes 32 consecutive floats of one row
+        // memory so that lane j then holds column chunk*32 + j of all 32 rows
 #pragma unroll
         for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
         __syncwarp();
         const int64_t col = col0 + chunk * 32 + lane;
-        if (col < n) {
-#pragma unroll 4
-          for (int rr = 0; rr < 32; ++rr) {
-            const int64_t row = row0 + rr;
-            if (row < m) epi.store(stage_rows[rr][lane], row, col);
-          }
+        if (col < n && rows > 0) {
+          float column[32];
+#pragma unroll
+          for (int rr = 0; rr < 32; ++rr) column[rr] = stage_rows[rr][lane];
+          epi.store_column(column, row0, col, rows);
         }
         __syncwarp();
       }

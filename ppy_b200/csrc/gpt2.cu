@@ -67,21 +67,37 @@ __global__ void __launch_bounds__(256) embed_kernel(const int64_t* __restrict__ 
 
 // ---------------------------------------------------------------- linear epilogues
 
+// tanh on the SFU (PTX tanh.approx.f32, max relative error about 2^-11): the GELU output is
+// rounded to bf16 (2^-8) right after, so the approximation does not show in it.
+__device__ __forceinline__ float tanh_sfu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float gelu_tanh(float z) {
   // 0.5 z (1 + tanh(sqrt(2/pi) (z + 0.044715 z^3))), GPT-2's activation
   const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-  return 0.5f * z * (1.0f + tanhf(u));
+  return 0.5f * z * (1.0f + tanh_sfu(u));
 }
 
+template <int ACTIVATION>  // 0 none, 1 GELU-tanh
 struct LinearBf16 {
   const float* bias;
   __nv_bfloat16* out;
   int64_t ldo;
-  int32_t activation;  // 0 none, 1 GELU-tanh
-  __device__ __forceinline__ void store(float acc, int64_t row, int64_t col) const {
-    float v = bias != nullptr ? acc + __ldg(bias + col) : acc;
-    if (activation == 1) v = gelu_tanh(v);
-    out[row * ldo + col] = __float2bfloat16_rn(v);
+  __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, int64_t col,
+                                               int64_t rows) const {
+    const float b = bias != nullptr ? __ldg(bias + col) : 0.f;
+    __nv_bfloat16* p = out + row0 * ldo + col;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      if (r < rows) {
+        float v = acc[r] + b;
+        if (ACTIVATION == 1) v = gelu_tanh(v);
+        p[r * ldo] = __float2bfloat16_rn(v);
+      }
+    }
   }
 };
 
@@ -89,9 +105,17 @@ struct LinearResidual {
   const float* bias;
   float* residual;  // read and written in place: residual += acc + bias
   int64_t ld;
-  __device__ __forceinline__ void store(float acc, int64_t row, int64_t col) const {
-    float* p = residual + row * ld + col;
-    *p = *p + (bias != nullptr ? acc + __ldg(bias + col) : acc);
+  __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, int64_t col,
+                                               int64_t rows) const {
+    const float b = bias != nullptr ? __ldg(bias + col) : 0.f;
+    float* p = residual + row0 * ld + col;
+    float old[32];
+    // all 32 loads first: the rows are independent, their latencies overlap
+#pragma unroll
+    for (int r = 0; r < 32; ++r) old[r] = r < rows ? p[r * ld] : 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      if (r < rows) p[r * ld] = old[r] + (acc[r] + b);
   }
 };
 
@@ -152,7 +176,7 @@ __device__ __forceinline__ void load_tile(uint8_t* tile, const __nv_bfloat16* sr
 // One CTA: 128 query rows of one (batch, head). Warp w owns rows 16w..16w+15; keys stream
 // through shared memory in tiles of 64 (double-buffered cp.async), scores and the softmax
 // are f32 (online: running max and sum per row), P is rounded to bf16 for the P.V product.
-__global__ void __launch_bounds__(THREADS) causal_kernel(const __nv_bfloat16* __restrict__ qkv,
+__global__ void __launch_bounds__(THREADS, 2) causal_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                          __nv_bfloat16* __restrict__ out,
                                                          int64_t batch, int64_t length,
                                                          int64_t heads, float scale_log2) {
@@ -328,16 +352,23 @@ int32_t ppyb200_linear_bf16(const uint16_t* a, const uint16_t* w, const float* b
                             uint16_t* out, int64_t m, int64_t n, int64_t k, int32_t activation,
                             int32_t* status) {
   if (m <= 0 || n <= 0) return PPYB200_OK;
-  LinearBf16 epi{bias, reinterpret_cast<__nv_bfloat16*>(out), n, activation};
   const auto* A = reinterpret_cast<const __nv_bfloat16*>(a);
   const auto* W = reinterpret_cast<const __nv_bfloat16*>(w);
-  if (!ppyb200::gemm::tileable(m, n, k) || !aligned16(a) || !aligned16(w)) {
-    ppyb200_set_error("ppyb200_linear_bf16: K % 64 and 16-byte aligned operands required");
+  if (!ppyb200::gemm::tileable(m, n, k) || !aligned16(a) || !aligned16(w) ||
+      (activation != 0 && activation != 1)) {
+    ppyb200_set_error("ppyb200_linear_bf16: K % 64, 16-byte aligned operands and an "
+                      "activation of 0 or 1 required");
     return PPYB200_RAISED;
   }
-  return finish(ppyb200::gemm::launch(A, W, m, n, k, epi, status, ppyb200_sm_count(),
-                                      stream_now()),
-                "ppyb200_linear_bf16", 1);
+  auto* O = reinterpret_cast<__nv_bfloat16*>(out);
+  cudaError_t e;
+  if (activation == 1)
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16<1>{bias, O, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  else
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16<0>{bias, O, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  return finish(e, "ppyb200_linear_bf16", 1);
 }
 
 int32_t ppyb200_linear_residual(const uint16_t* a, const uint16_t* w, const float* bias,

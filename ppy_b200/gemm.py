@@ -74,6 +74,10 @@ def matmul_launch(kernel: P.MatmulKernel, fn: P.TensorFunction, src) -> dict:
         "  __device__ __forceinline__ void store(float acc, int64_t row, int64_t col) const {"
         ] + body + [
         f"    out[row * n + col] = ppyb200::convert<{out_ct}, {result_ct}>({out.var});",
+        "  }",
+        "  __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, "
+        "int64_t col, int64_t rows) const {",
+        "    ppyb200::gemm::for_column(*this, acc, row0, col, rows);",
         "  }", "};"]
     src.kernels.append("\n".join(functor))
     # --- launch
