@@ -1,0 +1,67 @@
+"""Single-kernel cases for Nsight Compute: each runs one hand-written kernel a few times on
+seeded inputs of the benchmark's shapes, so `ncu -k <kernel> -s <warm-up> -c 1` can capture
+one launch of it alone.
+
+    python -m ppy_b200.profile_cases gemm        # matmul_bf16_kernel, 8192^3, K-major B
+    python -m ppy_b200.profile_cases attention   # causal_kernel, batch 4 x 1024, 12 heads
+    python -m ppy_b200.profile_cases fc          # matmul_bf16_kernel, GELU epilogue, GPT-2 FC
+    python -m ppy_b200.profile_cases lm_head     # matmul_bf16_kernel, N = 50257 logits
+
+Each case launches its kernel three times (two warm-ups, then the one to capture: `-s 2`).
+"""
+
+from __future__ import annotations
+
+import argparse
+
+
+def main() -> None:
+    import torch
+
+    from . import gpt2, runtime
+
+    parser = argparse.ArgumentParser()
+    parser.add_argument("case", choices=["gemm", "attention", "fc", "lm_head"])
+    case = parser.parse_args().case
+    runtime.init(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    runtime.set_stream(stream)
+    lib = runtime.library()
+    gpt2._bind(lib)
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def rand(*shape, dtype=torch.bfloat16):
+        return torch.randn(*shape, device="cuda", generator=g).to(dtype)
+
+    for _ in range(3):
+        if case in ("gemm", "lm_head"):
+            if not hasattr(main, "operands"):
+                m, n, k = (8192, 8192, 8192) if case == "gemm" else (4096, 50257, 768)
+                main.operands = (rand(m, k), rand(n, k), torch.empty(m, n, device="cuda"), m, n, k)
+            a, bt, c, m, n, k = main.operands
+            status = lib.ppyb200_matmul_bf16_kmajor(a.data_ptr(), bt.data_ptr(), None,
+                                                    c.data_ptr(), m, n, k)
+        elif case == "attention":
+            if not hasattr(main, "operands"):
+                main.operands = (rand(4 * 1024, 3 * 768),
+                                 torch.empty(4 * 1024, 768, device="cuda", dtype=torch.bfloat16))
+            qkv, out = main.operands
+            status = lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), out.data_ptr(), 4, 1024,
+                                                       12, 64)
+        else:
+            if not hasattr(main, "operands"):
+                main.operands = (rand(32768, 768), rand(3072, 768),
+                                 torch.zeros(3072, device="cuda"),
+                                 torch.empty(32768, 3072, device="cuda", dtype=torch.bfloat16))
+            h, w, b, f = main.operands
+            status = lib.ppyb200_linear_bf16(h.data_ptr(), w.data_ptr(), b.data_ptr(),
+                                             f.data_ptr(), 32768, 3072, 768, 1, None)
+        if status != 0:
+            raise SystemExit(f"{case}: {runtime.last_error()}")
+    torch.cuda.synchronize()
+    print(f"{case}: ok")
+
+
+if __name__ == "__main__":
+    main()
