@@ -62,6 +62,21 @@ def _args():
 # ---------------------------------------------------------------- distributed plumbing
 
 
+def shard_range(lo: int, hi: int, world: int, rank: int) -> tuple[int, int]:
+    """Rank `rank`'s contiguous slice of [lo, hi): equal spans, the last one shorter."""
+    span = (hi - lo + world - 1) // world
+    start = min(hi, lo + rank * span)
+    return start, min(hi, start + span)
+
+
+def shard_batch(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Rank `rank`'s sequences [start, stop) of a batch that splits evenly."""
+    if batch % world:
+        raise SystemExit(f"a batch of {batch} does not split over {world} GPUs")
+    per = batch // world
+    return rank * per, (rank + 1) * per
+
+
 class Dist:
     def __init__(self, gpus: int) -> None:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -76,7 +91,7 @@ class Dist:
 
             import torch.distributed as dist
 
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
             self.pg = dist
 
     def barrier(self) -> None:
@@ -324,10 +339,7 @@ class Collatz(Workload):
     scaling = "strong"
 
     def inputs(self):
-        world, rank = self.dist.world, self.dist.rank
-        span = (COLLATZ_HI - 1 + world - 1) // world
-        self.lo = 1 + rank * span
-        self.hi = min(COLLATZ_HI, self.lo + span)
+        self.lo, self.hi = shard_range(1, COLLATZ_HI, self.dist.world, self.dist.rank)
         self.total_steps = None
 
     def config(self):
@@ -441,13 +453,10 @@ class Gpt2(Workload):
     def inputs(self):
         import torch
 
-        world, rank = self.dist.world, self.dist.rank
-        if self.BATCH % world:
-            raise SystemExit("the batch of 32 does not split over this many GPUs")
-        per = self.BATCH // world
+        start, stop = shard_batch(self.BATCH, self.dist.world, self.dist.rank)
         g = torch.Generator().manual_seed(0)
         ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
-        self.ids = ids[rank * per:(rank + 1) * per].contiguous()
+        self.ids = ids[start:stop].contiguous()
 
     def config(self):
         return {"workload": "gpt2_124m_forward", "batch": self.BATCH, "seq_len": self.LENGTH,

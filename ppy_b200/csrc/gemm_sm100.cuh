@@ -19,7 +19,8 @@
 // PPYB200_DEVICE_RAISED in the call's status word and raises the CTA's abort flag; every
 // role then leaves its loop, the loader waits (bounded) for the copies it issued, the MMA
 // thread waits (bounded) for its MMAs, and the TMEM is freed before the CTA exits.
-// No load uses cluster multicast (the kernel may run on several GPUs of one node).
+// Every TMA load fills only this CTA's own shared memory (the kernel may run on several GPUs
+// of one node).
 #pragma once
 
 #include <cuda.h>
