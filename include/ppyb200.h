@@ -151,10 +151,29 @@ int32_t ppyb200_linear_residual(const uint16_t *a, const uint16_t *w, const floa
                                 float *residual, int64_t m, int64_t n, int64_t k,
                                 int32_t *status);
 
+/* The fused QKV projection of gpt2.ppy:50-51 (`F.linear(h, w_qkv, b_qkv)` split into q, k, v
+ * heads) on tcgen05 tensor cores, written in the layouts ppyb200_attention_causal_vt_bf16
+ * reads: q and k as bf16 into qkv [m, 3*heads*64] (its v columns are not written), v as bf16
+ * transposed per head into vt [batch*heads*64, length]: vt[((b*heads + h)*64 + d)*length + l]
+ * = v of token b*length + l, head h, dimension d. m = batch*length whole sequences,
+ * length % 32 == 0, K % 64 == 0, w [3*heads*64, K]. */
+int32_t ppyb200_linear_qkv_bf16(const uint16_t *a, const uint16_t *w, const float *bias,
+                                uint16_t *qkv, uint16_t *vt, int64_t m, int64_t k,
+                                int64_t length, int64_t heads, int32_t *status);
+
 /* Causal self-attention, F.scaled_dot_product_attention(q, k, v, is_causal=True) of
- * gpt2.ppy:52: qkv is [batch*length, 3*heads*64] bf16 (q, k, v side by side, head h at
- * columns h*64), out is [batch*length, heads*64] bf16 (heads merged, as gpt2.ppy:53).
- * Scores and softmax in f32. head_dim 64, length % 128 == 0. */
+ * gpt2.ppy:52, on tcgen05 tensor cores (S = Q K^T and O += P V in tensor memory, f32 online
+ * softmax): q, k from qkv [batch*length, 3*heads*64] (head h at columns h*64 of each), v from
+ * vt as ppyb200_linear_qkv_bf16 writes it; out [batch*length, heads*64] bf16 (heads merged,
+ * as gpt2.ppy:53). head_dim 64, length % 128 == 0. `*status` (may be NULL) is raised to 2 if
+ * the kernel gives up a bounded wait. */
+int32_t ppyb200_attention_causal_vt_bf16(const uint16_t *qkv, const uint16_t *vt, uint16_t *out,
+                                         int64_t batch, int64_t length, int64_t heads,
+                                         int64_t head_dim, int32_t *status);
+
+/* The same attention from qkv alone (q, k, v side by side): v is first transposed into the
+ * scratch arena; a bounded wait given up raises the call's status word
+ * (ppyb200_status_word). */
 int32_t ppyb200_attention_causal_bf16(const uint16_t *qkv, uint16_t *out, int64_t batch,
                                       int64_t length, int64_t heads, int64_t head_dim);
 

@@ -5,14 +5,17 @@
 //
 // Layouts: activations row-major [tokens, width] with token t = b * length + l; the residual
 // stream in f32, GEMM operands in bf16; weights as torch.nn.Linear keeps them, [out, in]
-// (K-major for the tensor cores); the fused QKV projection writes [tokens, 3 * width] with q,
-// k, v side by side, head h at columns h * head_dim of each.
+// (K-major for the tensor cores); the fused QKV projection writes q and k into
+// [tokens, 3 * width] (q, k, v side by side, head h at columns h * head_dim of each) and v
+// transposed per head into [batch * heads * head_dim, length], the layouts the tensor-core
+// attention kernel reads (attention_sm100.cuh).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <math.h>
 #include <stdint.h>
 
 #include "../../include/ppyb200.h"
+#include "attention_sm100.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_simt.cuh"
 #include "ppyb200_device.cuh"
@@ -121,213 +124,67 @@ struct LinearResidual {
 
 // ---------------------------------------------------------------- causal attention
 
-namespace attn {
+// The fused QKV projection's epilogue: q and k columns go to qkv [tokens, 3 * width] as bf16
+// (the v columns there are left alone); v goes out transposed per head,
+// vt[((b * heads + h) * 64 + d) * length + l], keys contiguous, which is the K-major B operand
+// of the attention kernel's P.V product. A column of 32 rows (one batch: length % 32 == 0)
+// is 64 contiguous bytes of vt.
+struct LinearQkv {
+  const float* bias;
+  __nv_bfloat16* qkv;
+  __nv_bfloat16* vt;
+  int64_t width, length, heads;
+  __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, int64_t col,
+                                               int64_t rows) const {
+    const float b = bias != nullptr ? __ldg(bias + col) : 0.f;
+    if (col < 2 * width) {
+      __nv_bfloat16* p = qkv + row0 * 3 * width + col;
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        if (r < rows) p[r * 3 * width] = __float2bfloat16_rn(acc[r] + b);
+      return;
+    }
+    const int64_t hd = col - 2 * width;
+    const int64_t bi = row0 / length, l0 = row0 - bi * length;
+    uint4* dst = reinterpret_cast<uint4*>(vt + ((bi * heads + (hd >> 6)) * 64 + (hd & 63)) * length +
+                                          l0);
+#pragma unroll
+    for (int r = 0; r < 32; r += 8) {
+      uint4 packed;
+      packed.x = ppyb200::attention::pack(acc[r + 0] + b, acc[r + 1] + b);
+      packed.y = ppyb200::attention::pack(acc[r + 2] + b, acc[r + 3] + b);
+      packed.z = ppyb200::attention::pack(acc[r + 4] + b, acc[r + 5] + b);
+      packed.w = ppyb200::attention::pack(acc[r + 6] + b, acc[r + 7] + b);
+      dst[r / 8] = packed;
+    }
+  }
+};
 
-constexpr int D = 64;     // head dim
-constexpr int BQ = 128;   // query rows per CTA (8 warps x 16)
-constexpr int BKV = 64;   // keys per tile
-constexpr int THREADS = 256;
-constexpr int TILE_Q_BYTES = BQ * D * 2;
-constexpr int TILE_KV_BYTES = BKV * D * 2;
-constexpr int SMEM_BYTES = TILE_Q_BYTES + 4 * TILE_KV_BYTES;  // Q, K[2], V[2]
-
-// byte offset of (row, 8-element chunk) in a [rows][64] bf16 tile: 16-byte chunks XOR-swizzled
-// by the row so that 8 consecutive rows of one chunk fall in 8 different bank groups
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// Copy `rows` x 64 bf16 (row stride `ld` elements) into a swizzled tile.
-__device__ __forceinline__ void load_tile(uint8_t* tile, const __nv_bfloat16* src, int rows,
-                                          int64_t ld) {
-  for (int i = threadIdx.x; i < rows * 8; i += THREADS) {
-    const int row = i >> 3, chunk = i & 7;
-    ppyb200::cp_async16(tile + swz(row, chunk), src + row * ld + chunk * 8);
+// vt[(bh * 64 + d) * length + l] = qkv[(b * length + l) * 3 * width + 2 * width + h * 64 + d]:
+// one CTA turns a [64 keys][64 d] block through shared memory (rows padded to 66 elements).
+__global__ void __launch_bounds__(256) v_transpose_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                          __nv_bfloat16* __restrict__ vt,
+                                                          int64_t length, int64_t heads) {
+  __shared__ __nv_bfloat16 tile[64][66];
+  const int64_t width = heads * 64;
+  const int64_t bh = blockIdx.x, b = bh / heads, h = bh % heads;
+  const int64_t l0 = (int64_t)blockIdx.y * 64;
+  for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+    const int l = i >> 5, d2 = (i & 31) * 2;
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(
+        qkv + (b * length + l0 + l) * 3 * width + 2 * width + h * 64 + d2);
+    tile[l][d2] = v.x;
+    tile[l][d2 + 1] = v.y;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+    const int d = i >> 5, l2 = (i & 31) * 2;
+    __nv_bfloat162 v;
+    v.x = tile[l2][d];
+    v.y = tile[l2 + 1][d];
+    *reinterpret_cast<__nv_bfloat162*>(vt + (bh * 64 + d) * length + l0 + l2) = v;
   }
 }
-
-// One CTA: 128 query rows of one (batch, head). Warp w owns rows 16w..16w+15; keys stream
-// through shared memory in tiles of 64 (double-buffered cp.async), scores and the softmax
-// are f32 (online: running max and sum per row), P is rounded to bf16 for the P.V product.
-__global__ void __launch_bounds__(THREADS, 2) causal_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                         __nv_bfloat16* __restrict__ out,
-                                                         int64_t batch, int64_t length,
-                                                         int64_t heads, float scale_log2) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sq = smem;
-  uint8_t* sk[2] = {smem + TILE_Q_BYTES, smem + TILE_Q_BYTES + TILE_KV_BYTES};
-  uint8_t* sv[2] = {smem + TILE_Q_BYTES + 2 * TILE_KV_BYTES,
-                    smem + TILE_Q_BYTES + 3 * TILE_KV_BYTES};
-  const int64_t q_tiles = length / BQ;
-  const int64_t bh_count = batch * heads;
-  // the longest (last) query tiles first: they have the most key tiles
-  const int64_t qt = q_tiles - 1 - (int64_t)blockIdx.x / bh_count;
-  const int64_t bh = (int64_t)blockIdx.x % bh_count;
-  const int64_t b = bh / heads, h = bh % heads;
-  const int64_t width = heads * D, ld = 3 * width;
-  const int64_t q0 = qt * BQ;
-  const __nv_bfloat16* base = qkv + (b * length) * ld + h * D;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-
-  const int kv_tiles = (int)((q0 + BQ) / BKV);
-  load_tile(sq, base + q0 * ld, BQ, ld);
-  load_tile(sk[0], base + width, BKV, ld);
-  load_tile(sv[0], base + 2 * width, BKV, ld);
-  ppyb200::cp_async_commit();
-
-  uint32_t qa[4][4];
-  float o[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
-  const int64_t q_lo = q0 + warp * 16 + g, q_hi = q_lo + 8;
-  const uint32_t sq_u = static_cast<uint32_t>(__cvta_generic_to_shared(sq));
-
-  for (int j = 0; j < kv_tiles; ++j) {
-    if (j + 1 < kv_tiles) {
-      load_tile(sk[(j + 1) & 1], base + (int64_t)(j + 1) * BKV * ld + width, BKV, ld);
-      load_tile(sv[(j + 1) & 1], base + (int64_t)(j + 1) * BKV * ld + 2 * width, BKV, ld);
-    }
-    ppyb200::cp_async_commit();
-    ppyb200::cp_async_wait<1>();
-    __syncthreads();
-    if (j == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int row = warp * 16 + (lane & 15), chunk = ks * 2 + (lane >> 4);
-        ldsm_x4(sq_u + swz(row, chunk), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
-      }
-    }
-    const uint32_t sk_u = static_cast<uint32_t>(__cvta_generic_to_shared(sk[j & 1]));
-    const uint32_t sv_u = static_cast<uint32_t>(__cvta_generic_to_shared(sv[j & 1]));
-    // S = Q K^T for this warp's 16 rows and the tile's 64 keys
-    float s[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int key = p * 16 + (lane & 7) + ((lane >> 4) << 3);
-        const int chunk = ks * 2 + ((lane >> 3) & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(sk_u + swz(key, chunk), b0, b1, b2, b3);
-        mma16816(s[2 * p], qa[ks], b0, b1);
-        mma16816(s[2 * p + 1], qa[ks], b2, b3);
-      }
-    }
-    // scale into log2 units, mask keys after the query, and the online softmax
-    const int64_t k0 = (int64_t)j * BKV;
-    const bool diagonal = k0 + BKV > q0;
-    float mx_lo = m_lo, mx_hi = m_hi;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int64_t key = k0 + nb * 8 + 2 * t + e;
-        float lo = s[nb][e] * scale_log2, hi = s[nb][2 + e] * scale_log2;
-        if (diagonal) {
-          if (key > q_lo) lo = -INFINITY;
-          if (key > q_hi) hi = -INFINITY;
-        }
-        s[nb][e] = lo;
-        s[nb][2 + e] = hi;
-        mx_lo = fmaxf(mx_lo, lo);
-        mx_hi = fmaxf(mx_hi, hi);
-      }
-    }
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-    const float keep_lo = exp2f(m_lo - mx_lo), keep_hi = exp2f(m_hi - mx_hi);
-    m_lo = mx_lo;
-    m_hi = mx_hi;
-    float sum_lo = 0.f, sum_hi = 0.f;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        s[nb][e] = exp2f(s[nb][e] - m_lo);
-        s[nb][2 + e] = exp2f(s[nb][2 + e] - m_hi);
-        sum_lo += s[nb][e];
-        sum_hi += s[nb][2 + e];
-      }
-    }
-    l_lo = l_lo * keep_lo + sum_lo;
-    l_hi = l_hi * keep_hi + sum_hi;
-#pragma unroll
-    for (int db = 0; db < 8; ++db) {
-      o[db][0] *= keep_lo;
-      o[db][1] *= keep_lo;
-      o[db][2] *= keep_hi;
-      o[db][3] *= keep_hi;
-    }
-    // O += P V: P's accumulator layout is the A operand layout of the next product
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-        const int chunk = p * 2 + (lane >> 4);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(sv_u + swz(key, chunk), b0, b1, b2, b3);
-        mma16816(o[2 * p], pa, b0, b1);
-        mma16816(o[2 * p + 1], pa, b2, b3);
-      }
-    }
-    __syncthreads();  // every warp is done with this tile before it is refilled
-  }
-  ppyb200::cp_async_wait<0>();
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-  const float inv_lo = 1.f / l_lo, inv_hi = 1.f / l_hi;
-  __nv_bfloat16* row_lo = out + (b * length + q_lo) * width + h * D;
-  __nv_bfloat16* row_hi = out + (b * length + q_hi) * width + h * D;
-#pragma unroll
-  for (int db = 0; db < 8; ++db) {
-    const int col = db * 8 + 2 * t;
-    *reinterpret_cast<uint32_t*>(row_lo + col) = pack_bf16(o[db][0] * inv_lo, o[db][1] * inv_lo);
-    *reinterpret_cast<uint32_t*>(row_hi + col) = pack_bf16(o[db][2] * inv_hi, o[db][3] * inv_hi);
-  }
-}
-
-}  // namespace attn
 
 }  // namespace
 
@@ -386,28 +243,63 @@ int32_t ppyb200_linear_residual(const uint16_t* a, const uint16_t* w, const floa
                 "ppyb200_linear_residual", 1);
 }
 
+int32_t ppyb200_linear_qkv_bf16(const uint16_t* a, const uint16_t* w, const float* bias,
+                                uint16_t* qkv, uint16_t* vt, int64_t m, int64_t k,
+                                int64_t length, int64_t heads, int32_t* status) {
+  if (m <= 0) return PPYB200_OK;
+  const int64_t width = heads * 64, n = 3 * width;
+  if (heads <= 0 || length <= 0 || length % 32 != 0 || m % length != 0 ||
+      !ppyb200::gemm::tileable(m, n, k) || !aligned16(a) || !aligned16(w) || !aligned16(qkv) ||
+      !aligned16(vt)) {
+    ppyb200_set_error("ppyb200_linear_qkv_bf16: K % 64, length % 32, whole sequences and "
+                      "16-byte aligned buffers required");
+    return PPYB200_RAISED;
+  }
+  LinearQkv epi{bias, reinterpret_cast<__nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(vt),
+                width, length, heads};
+  return finish(ppyb200::gemm::launch(reinterpret_cast<const __nv_bfloat16*>(a),
+                                      reinterpret_cast<const __nv_bfloat16*>(w), m, n, k, epi,
+                                      status, ppyb200_sm_count(), stream_now()),
+                "ppyb200_linear_qkv_bf16", 1);
+}
+
+int32_t ppyb200_attention_causal_vt_bf16(const uint16_t* qkv, const uint16_t* vt, uint16_t* out,
+                                         int64_t batch, int64_t length, int64_t heads,
+                                         int64_t head_dim, int32_t* status) {
+  if (batch <= 0 || length <= 0 || heads <= 0) return PPYB200_OK;
+  if (!ppyb200::attention::tileable(batch, length, heads, head_dim) || !aligned16(qkv) ||
+      !aligned16(vt) || !aligned16(out)) {
+    ppyb200_set_error("ppyb200_attention_causal_vt_bf16: head_dim 64, length a multiple of 128 "
+                      "and 16-byte aligned buffers required");
+    return PPYB200_RAISED;
+  }
+  return finish(ppyb200::attention::launch(reinterpret_cast<const __nv_bfloat16*>(qkv),
+                                           reinterpret_cast<const __nv_bfloat16*>(vt),
+                                           reinterpret_cast<__nv_bfloat16*>(out), batch, length,
+                                           heads, status, ppyb200_sm_count(), stream_now()),
+                "ppyb200_attention_causal_vt_bf16", 1);
+}
+
 int32_t ppyb200_attention_causal_bf16(const uint16_t* qkv, uint16_t* out, int64_t batch,
                                       int64_t length, int64_t heads, int64_t head_dim) {
   if (batch <= 0 || length <= 0 || heads <= 0) return PPYB200_OK;
-  if (head_dim != attn::D || length % attn::BQ != 0 || !aligned16(qkv) || !aligned16(out)) {
+  if (!ppyb200::attention::tileable(batch, length, heads, head_dim) || !aligned16(qkv) ||
+      !aligned16(out)) {
     ppyb200_set_error("ppyb200_attention_causal_bf16: head_dim 64, length a multiple of 128 and "
                       "16-byte aligned buffers required");
     return PPYB200_RAISED;
   }
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn::causal_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         attn::SMEM_BYTES);
-    if (e != cudaSuccess) return ppyb200_check((int32_t)e, "attention: shared memory");
-    configured = true;
-  }
-  const int64_t blocks = batch * heads * (length / attn::BQ);
-  const float scale_log2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-  attn::causal_kernel<<<(unsigned)blocks, attn::THREADS, attn::SMEM_BYTES, stream_now()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(out), batch,
-      length, heads, scale_log2);
-  return finish(cudaGetLastError(), "ppyb200_attention_causal_bf16", 1);
+  int32_t* status = ppyb200_status_word();
+  void* vt = ppyb200_scratch(batch * heads * 64 * length * 2);
+  if (status == nullptr || vt == nullptr) return PPYB200_RAISED;
+  const dim3 grid((unsigned)(batch * heads), (unsigned)(length / 64));
+  v_transpose_kernel<<<grid, 256, 0, stream_now()>>>(reinterpret_cast<const __nv_bfloat16*>(qkv),
+                                                     reinterpret_cast<__nv_bfloat16*>(vt), length,
+                                                     heads);
+  const int32_t s = finish(cudaGetLastError(), "ppyb200_attention_causal_bf16 (v transpose)", 1);
+  if (s != PPYB200_OK) return s;
+  return ppyb200_attention_causal_vt_bf16(qkv, reinterpret_cast<const uint16_t*>(vt), out, batch,
+                                          length, heads, head_dim, status);
 }
 
 }  // extern "C"

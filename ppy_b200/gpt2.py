@@ -6,8 +6,9 @@ of the forward is one of this package's kernels, called through the C ABI:
     embed (gather)                         ppyb200_gpt2_embed
     per block: layernorm -> bf16           the row kernel the backend builds from
                                            tests/golden/gpt2_layernorm.ppyir
-               QKV = h Wqkv^T + b          ppyb200_linear_bf16 (tcgen05)
-               causal attention            ppyb200_attention_causal_bf16
+               QKV = h Wqkv^T + b          ppyb200_linear_qkv_bf16 (tcgen05; q, k as is,
+                                           v transposed per head)
+               causal attention            ppyb200_attention_causal_vt_bf16 (tcgen05)
                x += a Wo^T + b             ppyb200_linear_residual (tcgen05, residual in place)
                layernorm -> bf16
                f = gelu(n Wfc^T + b)       ppyb200_linear_bf16 (GELU-tanh epilogue)
@@ -56,10 +57,13 @@ def _bind(lib) -> None:
     lib.ppyb200_gpt2_embed.argtypes = [p, p, p, p, i64, i64, i64, i64, p]
     lib.ppyb200_linear_bf16.argtypes = [p, p, p, p, i64, i64, i64, i32, p]
     lib.ppyb200_linear_residual.argtypes = [p, p, p, p, i64, i64, i64, p]
+    lib.ppyb200_linear_qkv_bf16.argtypes = [p, p, p, p, p, i64, i64, i64, i64, p]
     lib.ppyb200_attention_causal_bf16.argtypes = [p, p, i64, i64, i64, i64]
+    lib.ppyb200_attention_causal_vt_bf16.argtypes = [p, p, p, i64, i64, i64, i64, p]
     lib.ppyb200_matmul_bf16_kmajor.argtypes = [p, p, p, p, i64, i64, i64]
     for name in ("ppyb200_gpt2_embed", "ppyb200_linear_bf16", "ppyb200_linear_residual",
-                 "ppyb200_attention_causal_bf16", "ppyb200_matmul_bf16_kmajor"):
+                 "ppyb200_linear_qkv_bf16", "ppyb200_attention_causal_bf16",
+                 "ppyb200_attention_causal_vt_bf16", "ppyb200_matmul_bf16_kmajor"):
         getattr(lib, name).restype = i32
     lib._gpt2_bound = True
 
@@ -113,6 +117,7 @@ class GPT2:
                 "x": torch.empty(tokens, c, dtype=torch.float32, device=d),
                 "h": torch.empty(tokens, c, dtype=torch.bfloat16, device=d),
                 "qkv": torch.empty(tokens, 3 * c, dtype=torch.bfloat16, device=d),
+                "vt": torch.empty(tokens * c, dtype=torch.bfloat16, device=d),
                 "att": torch.empty(tokens, c, dtype=torch.bfloat16, device=d),
                 "f": torch.empty(tokens, 4 * c, dtype=torch.bfloat16, device=d),
                 "status": torch.zeros(1, dtype=torch.int32, device=d),
@@ -136,7 +141,8 @@ class GPT2:
             raise runtime.B200Error("the sequence length is a multiple of 128 up to the context")
         ids = ids.contiguous()
         s = self._scratch(tokens)
-        x, h, qkv, att, f, status = s["x"], s["h"], s["qkv"], s["att"], s["f"], s["status"]
+        x, h, qkv, vt, att, f = s["x"], s["h"], s["qkv"], s["vt"], s["att"], s["f"]
+        status = s["status"]
         if logits is None:
             logits = torch.empty(batch, length, v, dtype=torch.float32, device=self.device)
         lib = self.lib
@@ -148,11 +154,13 @@ class GPT2:
         ln = self.layernorm.device.layernorm_bf16
         for blk in self.blocks:
             self._check(ln(x, blk["ln1_g"], blk["ln1_b"], h).status, "layernorm")
-            self._check(lib.ppyb200_linear_bf16(h.data_ptr(), blk["w_qkv"].data_ptr(),
-                                                blk["b_qkv"].data_ptr(), qkv.data_ptr(), tokens,
-                                                3 * c, c, 0, st), "qkv")
-            self._check(lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), att.data_ptr(), batch,
-                                                          length, cfg.heads, cfg.head_dim),
+            self._check(lib.ppyb200_linear_qkv_bf16(h.data_ptr(), blk["w_qkv"].data_ptr(),
+                                                    blk["b_qkv"].data_ptr(), qkv.data_ptr(),
+                                                    vt.data_ptr(), tokens, c, length, cfg.heads,
+                                                    st), "qkv")
+            self._check(lib.ppyb200_attention_causal_vt_bf16(qkv.data_ptr(), vt.data_ptr(),
+                                                             att.data_ptr(), batch, length,
+                                                             cfg.heads, cfg.head_dim, st),
                         "attention")
             self._check(lib.ppyb200_linear_residual(att.data_ptr(), blk["w_o"].data_ptr(),
                                                     blk["b_o"].data_ptr(), x.data_ptr(), tokens,
@@ -198,7 +206,8 @@ class GPT2:
                 return result
             return timed
 
-        names = {"ppyb200_gpt2_embed": "embed", "ppyb200_attention_causal_bf16": "attention",
+        names = {"ppyb200_gpt2_embed": "embed", "ppyb200_linear_qkv_bf16": "qkv",
+                 "ppyb200_attention_causal_vt_bf16": "attention",
                  "ppyb200_matmul_bf16_kmajor": "lm_head"}
         for symbol, name in names.items():
             original[symbol] = getattr(lib, symbol)
@@ -211,7 +220,7 @@ class GPT2:
         shim = _Lib()
         for symbol, name in names.items():
             setattr(shim, symbol, wrap(name, original[symbol]))
-        shim.ppyb200_linear_bf16 = lambda *a: wrap("fc" if a[7] == 1 else "qkv", linear)(*a)
+        shim.ppyb200_linear_bf16 = lambda *a: wrap("fc", linear)(*a)
         shim.ppyb200_linear_residual = lambda *a: wrap(
             "proj" if a[6] == 4 * c else "out", residual)(*a)
         ln = self.layernorm

@@ -3,7 +3,7 @@ seeded inputs of the benchmark's shapes, so `ncu -k <kernel> -s <warm-up> -c 1` 
 one launch of it alone.
 
     python -m ppy_b200.profile_cases gemm        # matmul_bf16_kernel, 8192^3, K-major B
-    python -m ppy_b200.profile_cases attention   # causal_kernel, batch 4 x 1024, 12 heads
+    python -m ppy_b200.profile_cases attention   # causal_kernel, batch 32 x 1024, 12 heads
     python -m ppy_b200.profile_cases fc          # matmul_bf16_kernel, GELU epilogue, GPT-2 FC
     python -m ppy_b200.profile_cases lm_head     # matmul_bf16_kernel, N = 50257 logits
 
@@ -44,11 +44,11 @@ def main() -> None:
                                                     c.data_ptr(), m, n, k)
         elif case == "attention":
             if not hasattr(main, "operands"):
-                main.operands = (rand(4 * 1024, 3 * 768),
-                                 torch.empty(4 * 1024, 768, device="cuda", dtype=torch.bfloat16))
-            qkv, out = main.operands
-            status = lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), out.data_ptr(), 4, 1024,
-                                                       12, 64)
+                main.operands = (rand(32 * 1024, 3 * 768), rand(32 * 12 * 64, 1024),
+                                 torch.empty(32 * 1024, 768, device="cuda", dtype=torch.bfloat16))
+            qkv, vt, out = main.operands
+            status = lib.ppyb200_attention_causal_vt_bf16(qkv.data_ptr(), vt.data_ptr(),
+                                                          out.data_ptr(), 32, 1024, 12, 64, None)
         else:
             if not hasattr(main, "operands"):
                 main.operands = (rand(32768, 768), rand(3072, 768),

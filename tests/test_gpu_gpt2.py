@@ -47,20 +47,77 @@ def _close_logits(out, ref, rel=2e-2):
     return worst, norm
 
 
-def test_attention_matches_sdpa(lib):
-    batch, length, heads, d = 2, 256, 12, 64
+def _sdpa(qkv, batch, length, heads, d=64):
     width = heads * d
+    q, k, v = qkv.float().split(width, dim=1)
+    shape = lambda t: t.reshape(batch, length, heads, d).transpose(1, 2)  # noqa: E731
+    ref = F.scaled_dot_product_attention(shape(q), shape(k), shape(v), is_causal=True)
+    return ref.transpose(1, 2).reshape(batch * length, width)
+
+
+@pytest.mark.parametrize("batch,length,heads", [(2, 256, 12), (1, 1024, 12), (3, 384, 5),
+                                                (1, 128, 1)])
+def test_attention_matches_sdpa(lib, batch, length, heads):
+    width = heads * 64
     g = torch.Generator(device="cuda").manual_seed(0)
     qkv = torch.randn(batch * length, 3 * width, device="cuda", generator=g).to(torch.bfloat16)
     out = torch.empty(batch * length, width, device="cuda", dtype=torch.bfloat16)
     assert lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), out.data_ptr(), batch, length,
-                                             heads, d) == 0
+                                             heads, 64) == 0
     torch.cuda.synchronize()
-    q, k, v = qkv.float().split(width, dim=1)
-    shape = lambda t: t.reshape(batch, length, heads, d).transpose(1, 2)  # noqa: E731
-    ref = F.scaled_dot_product_attention(shape(q), shape(k), shape(v), is_causal=True)
-    ref = ref.transpose(1, 2).reshape(batch * length, width)
-    _close(out, ref)  # P and the output rounded to bf16: ~1e-2 at worst
+    _close(out, _sdpa(qkv, batch, length, heads))  # P and the output rounded to bf16
+
+
+def test_attention_large_scores(lib):
+    # scores of a few hundred: the running max moves by large steps, rescaling O every tile
+    batch, length, heads = 1, 512, 2
+    g = torch.Generator(device="cuda").manual_seed(7)
+    qkv = (4 * torch.randn(batch * length, 3 * heads * 64, device="cuda", generator=g))
+    width = heads * 64
+    qkv[:, width:width + 64] += torch.arange(length, device="cuda").unsqueeze(1) / 8  # head 0 keys
+    qkv = qkv.to(torch.bfloat16)
+    out = torch.empty(batch * length, heads * 64, device="cuda", dtype=torch.bfloat16)
+    assert lib.ppyb200_attention_causal_bf16(qkv.data_ptr(), out.data_ptr(), batch, length,
+                                             heads, 64) == 0
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    _close(out, _sdpa(qkv, batch, length, heads), rel=3e-2)
+
+
+def test_qkv_projection_and_attention_from_vt(lib):
+    batch, length, heads, k = 2, 256, 12, 768
+    width = heads * 64
+    g = torch.Generator(device="cuda").manual_seed(8)
+    a = torch.randn(batch * length, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (0.05 * torch.randn(3 * width, k, device="cuda", generator=g)).to(torch.bfloat16)
+    b = 0.1 * torch.randn(3 * width, device="cuda", generator=g)
+    qkv = torch.zeros(batch * length, 3 * width, device="cuda", dtype=torch.bfloat16)
+    vt = torch.empty(batch * heads * 64, length, device="cuda", dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert lib.ppyb200_linear_qkv_bf16(a.data_ptr(), w.data_ptr(), b.data_ptr(), qkv.data_ptr(),
+                                       vt.data_ptr(), batch * length, k, length, heads,
+                                       status.data_ptr()) == 0
+    torch.cuda.synchronize()
+    ref = F.linear(a.float(), w.float(), b)
+    _close(qkv[:, :2 * width], ref[:, :2 * width], rel=1e-2)
+    assert not qkv[:, 2 * width:].any()  # the v columns are not written
+    v_ref = ref[:, 2 * width:].reshape(batch, length, heads, 64).permute(0, 2, 3, 1)
+    _close(vt, v_ref.reshape(batch * heads * 64, length), rel=1e-2)
+    # attention from q, k in qkv and v in vt = attention of the whole qkv
+    full = qkv.clone()
+    full[:, 2 * width:] = vt.reshape(batch, heads, 64, length).permute(0, 3, 1, 2).reshape(
+        batch * length, width)
+    out = torch.empty(batch * length, width, device="cuda", dtype=torch.bfloat16)
+    assert lib.ppyb200_attention_causal_vt_bf16(qkv.data_ptr(), vt.data_ptr(), out.data_ptr(),
+                                                batch, length, heads, 64,
+                                                status.data_ptr()) == 0
+    alone = torch.empty_like(out)
+    assert lib.ppyb200_attention_causal_bf16(full.data_ptr(), alone.data_ptr(), batch, length,
+                                             heads, 64) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(out, alone)
+    _close(out, _sdpa(full, batch, length, heads))
 
 
 def test_attention_refuses_lengths_off_the_tile(lib):
