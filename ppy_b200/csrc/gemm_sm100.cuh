@@ -28,6 +28,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "ppyb200_device.cuh"
 
 namespace ppyb200 {
@@ -193,6 +195,28 @@ __device__ __forceinline__ void tile_coords(int64_t t, int64_t m_blocks, int64_t
 // acc[r] at (row0 + r, col) for r < rows. `for_column` gives that from a per-element store.
 // (Every loop over the 32 values is unrolled in full: an index the compiler cannot resolve
 // would put the array in local memory.)
+// An epilogue may instead take whole rows: with `static constexpr bool kRows = true` the kernel
+// calls `store_row(const float (&acc)[32], int64_t row, int64_t col0, int64_t cols)` with acc[j]
+// at (row, col0 + j) for j < cols (cols = 32 except at a ragged right edge): the values a lane
+// reads from tensor memory, with no transpose, for epilogues whose rows it can write as 16-byte
+// vectors.
+//
+// Or it may take four consecutive columns of eight rows at a time: with
+// `static constexpr bool kQuads = true` the kernel calls
+// `store_quads(const float4 (&v)[8], int64_t row, int count, int64_t col)` with v[i] the four
+// values at (row + 4 i, col..col+3) for i < count (col % 4 == 0; all inside C when N % 4 == 0),
+// after turning the 32 x 32 block through shared memory so that eight lanes cover one row's
+// 128 bytes: every 16-byte access of the warp then covers four whole 128-byte rows. For f32
+// outputs whose rows start on 16-byte boundaries.
+template <class E, class = void>
+struct takes_rows : std::false_type {};
+template <class E>
+struct takes_rows<E, std::void_t<decltype(E::kRows)>> : std::integral_constant<bool, E::kRows> {};
+template <class E, class = void>
+struct takes_quads : std::false_type {};
+template <class E>
+struct takes_quads<E, std::void_t<decltype(E::kQuads)>> : std::integral_constant<bool, E::kQuads> {};
+
 template <class Epi>
 __device__ __forceinline__ void for_column(const Epi& epi, const float (&acc)[32], int64_t row0,
                                            int64_t col, int64_t rows) {
@@ -211,6 +235,26 @@ struct BiasEpilogue {
   __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, int64_t col,
                                                int64_t rows) const {
     for_column(*this, acc, row0, col, rows);
+  }
+};
+
+// The same four columns at a time, for C rows that start on 16-byte boundaries (ldc % 4 == 0,
+// N % 4 == 0, C and bias 16-byte aligned).
+struct BiasQuadEpilogue {
+  static constexpr bool kQuads = true;
+  const float* bias;
+  float* c;
+  int64_t ldc;
+  __device__ __forceinline__ void store_quads(const float4 (&v)[8], int64_t row, int count,
+                                              int64_t col) const {
+    const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    float* p = c + row * ldc + col;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < count)
+        __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc),
+               make_float4(v[i].x + b.x, v[i].y + b.y, v[i].z + b.z, v[i].w + b.w));
   }
 };
 
@@ -336,19 +380,51 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS + chunk * 32),
                   r);
-        // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
-        // memory so that lane j then holds column chunk*32 + j of all 32 rows
+        if constexpr (takes_rows<Epi>::value) {
+          // lane holds row (row0 + lane), columns chunk*32 .. +31, as the epilogue takes them
+          const int64_t col = col0 + chunk * 32;
+          if (lane < rows && col < n) {
+            float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
-        __syncwarp();
-        const int64_t col = col0 + chunk * 32 + lane;
-        if (col < n && rows > 0) {
-          float column[32];
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            epi.store_row(v, row0 + lane, col, n - col < 32 ? n - col : 32);
+          }
+        } else if constexpr (takes_quads<Epi>::value) {
+          // 32 rows x 8 float4 in shared memory, the float4 slot XOR-swizzled by the row so that
+          // both the row-wise writes and the column-wise reads are free of bank conflicts
+          float4* quad = reinterpret_cast<float4*>(&stage_rows[0][0]);
 #pragma unroll
-          for (int rr = 0; rr < 32; ++rr) column[rr] = stage_rows[rr][lane];
-          epi.store_column(column, row0, col, rows);
+          for (int q = 0; q < 8; ++q)
+            quad[lane * 8 + (q ^ (lane & 7))] =
+                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                            __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          __syncwarp();
+          const int64_t col = col0 + chunk * 32 + 4 * (lane & 7);
+          float4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = (lane >> 3) + 4 * i;
+            v[i] = quad[rr * 8 + ((lane & 7) ^ (rr & 7))];
+          }
+          __syncwarp();
+          // rows (lane >> 3) + 4 i inside C: i < (rows - (lane >> 3) + 3) / 4
+          const int count = rows > (lane >> 3) ? (int)((rows - (lane >> 3) + 3) / 4) : 0;
+          if (col < n && count > 0) epi.store_quads(v, row0 + (lane >> 3), count < 8 ? count : 8, col);
+        } else {
+          // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
+          // memory so that lane j then holds column chunk*32 + j of all 32 rows
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
+          __syncwarp();
+          const int64_t col = col0 + chunk * 32 + lane;
+          if (col < n && rows > 0) {
+            float column[32];
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) column[rr] = stage_rows[rr][lane];
+            epi.store_column(column, row0, col, rows);
+          }
+          __syncwarp();
         }
-        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();

@@ -122,41 +122,124 @@ struct LinearResidual {
   }
 };
 
+// Row and four-column forms of the epilogues above (gemm_sm100.cuh), for outputs whose rows
+// start on 16-byte boundaries: 16-byte loads and stores.
+__device__ __forceinline__ void load_bias32(const float* bias, int64_t col0, float (&b)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float4 v = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col0) + q)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    b[4 * q] = v.x;
+    b[4 * q + 1] = v.y;
+    b[4 * q + 2] = v.z;
+    b[4 * q + 3] = v.w;
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int ACTIVATION>
+struct LinearBf16Rows {  // ldo % 8 == 0, out and bias 16-byte aligned
+  static constexpr bool kRows = true;
+  const float* bias;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  __device__ __forceinline__ void store_row(const float (&acc)[32], int64_t row, int64_t col0,
+                                            int64_t cols) const {
+    __nv_bfloat16* p = out + row * ldo + col0;
+    if (cols == 32) {
+      float b[32];
+      load_bias32(bias, col0, b);
+      uint32_t pk[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        float v0 = acc[2 * k] + b[2 * k], v1 = acc[2 * k + 1] + b[2 * k + 1];
+        if (ACTIVATION == 1) {
+          v0 = gelu_tanh(v0);
+          v1 = gelu_tanh(v1);
+        }
+        pk[k] = pack_bf16x2(v0, v1);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        reinterpret_cast<uint4*>(p)[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                                                    pk[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < cols) {
+          float v = acc[j] + (bias != nullptr ? __ldg(bias + col0 + j) : 0.f);
+          if (ACTIVATION == 1) v = gelu_tanh(v);
+          p[j] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+  }
+};
+
+struct LinearResidualQuads {  // ld % 4 == 0, N % 4 == 0, residual and bias 16-byte aligned
+  static constexpr bool kQuads = true;
+  const float* bias;
+  float* residual;
+  int64_t ld;
+  __device__ __forceinline__ void store_quads(const float4 (&v)[8], int64_t row, int count,
+                                              int64_t col) const {
+    const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    float* p = residual + row * ld + col;
+    float4 old[8];
+    // all the loads first: their latencies overlap
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      old[i] = i < count ? *reinterpret_cast<const float4*>(p + 4 * i * ld)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < count)
+        *reinterpret_cast<float4*>(p + 4 * i * ld) =
+            make_float4(old[i].x + (v[i].x + b.x), old[i].y + (v[i].y + b.y),
+                        old[i].z + (v[i].z + b.z), old[i].w + (v[i].w + b.w));
+  }
+};
+
 // ---------------------------------------------------------------- causal attention
 
 // The fused QKV projection's epilogue: q and k columns go to qkv [tokens, 3 * width] as bf16
 // (the v columns there are left alone); v goes out transposed per head,
 // vt[((b * heads + h) * 64 + d) * length + l], keys contiguous, which is the K-major B operand
-// of the attention kernel's P.V product. A column of 32 rows (one batch: length % 32 == 0)
-// is 64 contiguous bytes of vt.
+// of the attention kernel's P.V product. The 32 rows a warp holds are consecutive tokens of one
+// sequence (length % 32 == 0), so each store of a v column covers 64 contiguous bytes of vt.
 struct LinearQkv {
+  static constexpr bool kRows = true;
   const float* bias;
   __nv_bfloat16* qkv;
   __nv_bfloat16* vt;
   int64_t width, length, heads;
-  __device__ __forceinline__ void store_column(const float (&acc)[32], int64_t row0, int64_t col,
-                                               int64_t rows) const {
-    const float b = bias != nullptr ? __ldg(bias + col) : 0.f;
-    if (col < 2 * width) {
-      __nv_bfloat16* p = qkv + row0 * 3 * width + col;
+  // a lane holds 32 consecutive columns of one token's row; the chunk lies inside q, k or one
+  // head of v (width and the head size are multiples of 32)
+  __device__ __forceinline__ void store_row(const float (&acc)[32], int64_t row, int64_t col0,
+                                            int64_t cols) const {
+    float b[32];
+    load_bias32(bias, col0, b);
+    if (col0 < 2 * width) {
+      uint32_t pk[16];
 #pragma unroll
-      for (int r = 0; r < 32; ++r)
-        if (r < rows) p[r * 3 * width] = __float2bfloat16_rn(acc[r] + b);
+      for (int k = 0; k < 16; ++k) pk[k] = pack_bf16x2(acc[2 * k] + b[2 * k], acc[2 * k + 1] + b[2 * k + 1]);
+      uint4* dst = reinterpret_cast<uint4*>(qkv + row * 3 * width + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       return;
     }
-    const int64_t hd = col - 2 * width;
-    const int64_t bi = row0 / length, l0 = row0 - bi * length;
-    uint4* dst = reinterpret_cast<uint4*>(vt + ((bi * heads + (hd >> 6)) * 64 + (hd & 63)) * length +
-                                          l0);
+    // v: column d of head h goes to vt row (b * heads + h) * 64 + d at position l; the lanes of
+    // a warp hold consecutive tokens, so each store covers 64 contiguous bytes
+    const int64_t hd = col0 - 2 * width;
+    const int64_t bi = row / length, l = row - bi * length;
+    __nv_bfloat16* dst = vt + ((bi * heads + (hd >> 6)) * 64 + (hd & 63)) * length + l;
 #pragma unroll
-    for (int r = 0; r < 32; r += 8) {
-      uint4 packed;
-      packed.x = ppyb200::attention::pack(acc[r + 0] + b, acc[r + 1] + b);
-      packed.y = ppyb200::attention::pack(acc[r + 2] + b, acc[r + 3] + b);
-      packed.z = ppyb200::attention::pack(acc[r + 4] + b, acc[r + 5] + b);
-      packed.w = ppyb200::attention::pack(acc[r + 6] + b, acc[r + 7] + b);
-      dst[r / 8] = packed;
-    }
+    for (int j = 0; j < 32; ++j) dst[j * length] = __float2bfloat16_rn(acc[j] + b[j]);
   }
 };
 
@@ -218,8 +301,15 @@ int32_t ppyb200_linear_bf16(const uint16_t* a, const uint16_t* w, const float* b
     return PPYB200_RAISED;
   }
   auto* O = reinterpret_cast<__nv_bfloat16*>(out);
+  const bool rows = n % 8 == 0 && aligned16(out) && (bias == nullptr || aligned16(bias));
   cudaError_t e;
-  if (activation == 1)
+  if (activation == 1 && rows)
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16Rows<1>{bias, O, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  else if (rows)
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16Rows<0>{bias, O, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  else if (activation == 1)
     e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16<1>{bias, O, n}, status,
                               ppyb200_sm_count(), stream_now());
   else
@@ -232,15 +322,20 @@ int32_t ppyb200_linear_residual(const uint16_t* a, const uint16_t* w, const floa
                                 float* residual, int64_t m, int64_t n, int64_t k,
                                 int32_t* status) {
   if (m <= 0 || n <= 0) return PPYB200_OK;
-  LinearResidual epi{bias, residual, n};
   if (!ppyb200::gemm::tileable(m, n, k) || !aligned16(a) || !aligned16(w)) {
     ppyb200_set_error("ppyb200_linear_residual: K % 64 and 16-byte aligned operands required");
     return PPYB200_RAISED;
   }
-  return finish(ppyb200::gemm::launch(reinterpret_cast<const __nv_bfloat16*>(a),
-                                      reinterpret_cast<const __nv_bfloat16*>(w), m, n, k, epi,
-                                      status, ppyb200_sm_count(), stream_now()),
-                "ppyb200_linear_residual", 1);
+  const auto* A = reinterpret_cast<const __nv_bfloat16*>(a);
+  const auto* W = reinterpret_cast<const __nv_bfloat16*>(w);
+  cudaError_t e;
+  if (n % 4 == 0 && aligned16(residual) && (bias == nullptr || aligned16(bias)))
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearResidualQuads{bias, residual, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  else
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearResidual{bias, residual, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  return finish(e, "ppyb200_linear_residual", 1);
 }
 
 int32_t ppyb200_linear_qkv_bf16(const uint16_t* a, const uint16_t* w, const float* bias,
@@ -250,9 +345,9 @@ int32_t ppyb200_linear_qkv_bf16(const uint16_t* a, const uint16_t* w, const floa
   const int64_t width = heads * 64, n = 3 * width;
   if (heads <= 0 || length <= 0 || length % 32 != 0 || m % length != 0 ||
       !ppyb200::gemm::tileable(m, n, k) || !aligned16(a) || !aligned16(w) || !aligned16(qkv) ||
-      !aligned16(vt)) {
+      !aligned16(vt) || (bias != nullptr && !aligned16(bias))) {
     ppyb200_set_error("ppyb200_linear_qkv_bf16: K % 64, length % 32, whole sequences and "
-                      "16-byte aligned buffers required");
+                      "16-byte aligned buffers (bias included) required");
     return PPYB200_RAISED;
   }
   LinearQkv epi{bias, reinterpret_cast<__nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(vt),
