@@ -52,7 +52,7 @@ def _args():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--workload", default="gelu",
-                   choices=["gelu", "rows", "collatz", "gemm", "gpt2"])
+                   choices=["gelu", "rows", "collatz", "gemm", "gpt2", "gpt2_tp"])
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU-baseline sample length (seconds of host work)")
@@ -513,6 +513,53 @@ class Gpt2(Workload):
         return float((got - ref).abs().max() / ref.abs().max())
 
 
+class Gpt2TP(Gpt2):
+    """The tensor-parallel variant: every rank works on the whole batch with 12/N heads,
+    3072/N hidden units and 50257/N logits columns; two all-reduces of the residual stream
+    per block (N in {1, 2, 4})."""
+
+    metric = "GPT-2-124M forward tokens/s, tensor parallel: batch 32 x 1024, logits out"
+    kernel = "gpt2_tp_forward"
+
+    def inputs(self):
+        import torch
+
+        g = torch.Generator().manual_seed(0)
+        self.ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
+
+    def config(self):
+        cfg = super().config()
+        cfg.update(workload="gpt2_124m_forward_tp", parallelism=f"tp{self.dist.world}",
+                   exchange="2 NCCL all-reduces (sum, f32 [32768, 768]) per block")
+        return cfg
+
+    def setup_device(self, runtime, torch):
+        from ppy_b200 import gpt2, gpt2_tp
+
+        self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0)
+        self.gpt2 = gpt2
+        self.dids = self.ids.cuda()
+        self.pids = self.ids.pin_memory()
+        v0, v1 = self.model.shard.vocab
+        self.logits = torch.empty(self.BATCH, self.LENGTH, v1 - v0, device="cuda")
+        self.last = torch.empty(self.BATCH, v1 - v0).pin_memory()
+
+    def h2d_d2h(self):
+        v0, v1 = self.model.shard.vocab
+        return 8 * self.BATCH * self.LENGTH, 4 * self.BATCH * (v1 - v0)
+
+    def check(self, oracle):
+        import torch
+
+        full = self.gpt2.GPT2(self.gpt2.GPT2_124M, seed=0)
+        ids = self.dids[:1, :256]
+        got = self.model.forward(ids)
+        v0, v1 = self.model.shard.vocab
+        ref = full.reference_forward(ids)[..., v0:v1]
+        torch.cuda.synchronize()
+        return float((got - ref).abs().max() / ref.abs().max())
+
+
 def _cpu_reference_model():
     """The GPT-2 forward of examples/46_gpt2/gpt2.ppy:18-57 (torch ATen ops) on the CPU, the
     same shapes and init, f32."""
@@ -546,7 +593,8 @@ def _cpu_reference_model():
     return forward
 
 
-WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz, "gemm": Gemm, "gpt2": Gpt2}
+WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz, "gemm": Gemm, "gpt2": Gpt2,
+             "gpt2_tp": Gpt2TP}
 
 
 def units_per_step(w: Workload) -> float:
@@ -583,6 +631,7 @@ def cpu_baseline(w: Workload, seconds: float) -> dict:
         if elapsed >= seconds:
             break
     sample = {"gpt2": "torch CPU forward (f32) of the first sequence (1 x 1024), repeated",
+              "gpt2_tp": "torch CPU forward (f32) of the first sequence (1 x 1024), repeated",
               "gemm": "NumPy f32 BLAS on the first 512 rows of A, repeated",
               "gelu": "first 2^22 elements of the batch, repeated",
               "rows": "first 4096 rows of the batch, repeated",
@@ -685,7 +734,9 @@ def run_b200(args, dist: Dist) -> None:
     if isinstance(w, Collatz):
         sums = dist.sum_i64([w.sum])
         units_all = float(sums[0])
-    if isinstance(w, Gpt2):
+    if isinstance(w, Gpt2TP):
+        units_all = float(units)  # every rank works on the same tokens
+    elif isinstance(w, Gpt2):
         units_all = float(dist.sum_i64([int(units)])[0])
     value = to_metric(w, units_all * args.steps, total_ms / 1e3)
     kernel_ms = float(np.mean(step_ms))
@@ -734,6 +785,15 @@ def run_b200(args, dist: Dist) -> None:
                                 "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                                 "traffic": traffic(w.kernel), "peak_source": pk["source"],
                                 "kernel": w.kernel, "kernel_ms": kernel_ms}
+        elif isinstance(w, Gpt2TP):
+            pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (
+                REPO / "MEASURED_PEAKS.json").exists() else 1400.0
+            per_gpu = w.gpt2.sequence_flops(w.gpt2.GPT2_124M, w.BATCH, w.LENGTH) / dist.world / (
+                total_ms / args.steps / 1e3) / 1e12
+            line["roofline"] = {"bound": "tensor", "achieved": per_gpu, "peak": pk_t,
+                                "unit": "TFLOP/s", "frac": per_gpu / pk_t, "traffic": None,
+                                "peak_source": "measured (sustained)", "kernel": w.kernel,
+                                "kernel_ms": total_ms / args.steps}
         elif isinstance(w, Gpt2):
             pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (
                 REPO / "MEASURED_PEAKS.json").exists() else 1400.0

@@ -1,0 +1,197 @@
+"""Tensor-parallel GPT-2 forward over g GPUs (one process per GPU; torch.distributed with NCCL
+for the exchange), the TP variant of the reference's GPT-2 example
+(examples/46_gpt2/gpt2.ppy:18-57, block; :210-241, forward).
+
+Each rank holds 12/g heads and 3072/g hidden units of every block and 50257/g rows of the tied
+LM head:
+
+    QKV projection   column-parallel: this rank's q, k, v heads (ppyb200_linear_qkv_bf16)
+    attention        on the local heads (ppyb200_attention_causal_vt_bf16)
+    out projection   row-parallel: rank 0 adds its partial product, the bias and the residual
+                     into x (ppyb200_linear_residual), the other ranks write their partial
+                     product into x (ppyb200_matmul_bf16_kmajor); one all-reduce (sum) of x
+    FC + GELU        column-parallel (ppyb200_linear_bf16, GELU epilogue)
+    proj             row-parallel, as the out projection; one all-reduce of x
+    layernorms       replicated on the full residual stream
+    LM head          vocab-parallel: this rank's slice of the logits
+
+Two all-reduces of the f32 residual stream [tokens, 768] per block. g divides 12 and the local
+widths (768/g and 3072/g) stay multiples of 64 (the tensor-core K step): g in {1, 2, 4}.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from . import runtime
+from .gpt2 import GPT2, GPT2_124M, Config, _bind
+
+__all__ = ["TPShard", "shard_ranges", "shard_block", "GPT2TensorParallel"]
+
+
+@dataclass(frozen=True)
+class TPShard:
+    """The slices rank `rank` of `size` holds."""
+
+    rank: int
+    size: int
+    heads: tuple[int, int]   # [first, last) head
+    hidden: tuple[int, int]  # [first, last) FC unit
+    vocab: tuple[int, int]   # [first, last) LM head row
+
+
+def shard_ranges(config: Config, rank: int, size: int) -> TPShard:
+    if size < 1 or not 0 <= rank < size:
+        raise ValueError(f"rank {rank} of {size}")
+    if config.heads % size or (config.width // size) % 64 or (4 * config.width // size) % 64:
+        raise ValueError(f"{size} ranks do not split {config.heads} heads and the widths "
+                         f"into 64-wide slices")
+    hl = config.heads // size
+    fl = 4 * config.width // size
+    per, extra = divmod(config.vocab, size)
+    v0 = rank * per + min(rank, extra)
+    return TPShard(rank, size, (rank * hl, (rank + 1) * hl), (rank * fl, (rank + 1) * fl),
+                   (v0, v0 + per + (1 if rank < extra else 0)))
+
+
+def shard_block(blk: dict, config: Config, shard: TPShard) -> dict:
+    """This rank's weights of one block (torch tensors on any device; [out, in] layouts):
+    w_qkv/b_qkv the local q, k, v heads side by side; w_o the local input columns; w_fc/b_fc
+    the local hidden units; w_proj the local input columns. Biases of the row-parallel layers
+    stay whole (rank 0 adds them once)."""
+    import torch
+
+    c, d = config.width, config.head_dim
+    h0, h1 = shard.heads
+    f0, f1 = shard.hidden
+    cols = slice(h0 * d, h1 * d)
+    parts = [slice(i * c + h0 * d, i * c + h1 * d) for i in range(3)]
+    return {
+        "ln1_g": blk["ln1_g"], "ln1_b": blk["ln1_b"],
+        "w_qkv": torch.cat([blk["w_qkv"][p] for p in parts]).contiguous(),
+        "b_qkv": torch.cat([blk["b_qkv"][p] for p in parts]).contiguous(),
+        "w_o": blk["w_o"][:, cols].contiguous(), "b_o": blk["b_o"],
+        "ln2_g": blk["ln2_g"], "ln2_b": blk["ln2_b"],
+        "w_fc": blk["w_fc"][f0:f1].contiguous(), "b_fc": blk["b_fc"][f0:f1].contiguous(),
+        "w_proj": blk["w_proj"][:, f0:f1].contiguous(), "b_proj": blk["b_proj"],
+    }
+
+
+class GPT2TensorParallel:
+    """This rank's part of a randomly initialised GPT-2 (the same weights as GPT2(config, seed)
+    on every rank, then sliced). Call forward on every rank of `group` with the same ids."""
+
+    def __init__(self, config: Config = GPT2_124M, seed: int = 0, group=None) -> None:
+        import torch
+        import torch.distributed as dist
+
+        self.config = config
+        self.group = group
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        size = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.shard = shard_ranges(config, rank, size)
+        full = GPT2(config, seed)
+        self.wte, self.wpe = full.wte, full.wpe
+        v0, v1 = self.shard.vocab
+        self.head = full.wte[v0:v1].contiguous()
+        self.blocks = [shard_block(b, config, self.shard) for b in full.blocks]
+        self.lnf_g, self.lnf_b = full.lnf_g, full.lnf_b
+        self.layernorm = full.layernorm
+        self.lib = runtime.library()
+        _bind(self.lib)
+        self._buffers: dict = {}
+        del full
+        torch.cuda.empty_cache()
+
+    def _scratch(self, tokens: int):
+        import torch
+
+        found = self._buffers.get(tokens)
+        if found is None:
+            c, d = self.config.width, "cuda"
+            hl = self.shard.heads[1] - self.shard.heads[0]
+            wl = hl * self.config.head_dim
+            fl = self.shard.hidden[1] - self.shard.hidden[0]
+            found = {
+                "x": torch.empty(tokens, c, dtype=torch.float32, device=d),
+                "h": torch.empty(tokens, c, dtype=torch.bfloat16, device=d),
+                "qkv": torch.empty(tokens, 3 * wl, dtype=torch.bfloat16, device=d),
+                "vt": torch.empty(tokens * wl, dtype=torch.bfloat16, device=d),
+                "att": torch.empty(tokens, wl, dtype=torch.bfloat16, device=d),
+                "f": torch.empty(tokens, fl, dtype=torch.bfloat16, device=d),
+                "status": torch.zeros(1, dtype=torch.int32, device=d),
+            }
+            self._buffers = {tokens: found}
+        return found
+
+    def _check(self, status: int, what: str) -> None:
+        if status != runtime.STATUS_OK:
+            raise runtime.B200Error(f"{what}: {runtime.last_error()}")
+
+    def _row_parallel(self, a, w, bias, x, tokens, k, st, what):
+        """x <- x + bias + sum over ranks of a_r @ w_r^T (rank 0 keeps x and the bias)."""
+        import torch.distributed as dist
+
+        c = self.config.width
+        if self.shard.rank == 0:
+            status = self.lib.ppyb200_linear_residual(a.data_ptr(), w.data_ptr(), bias.data_ptr(),
+                                                      x.data_ptr(), tokens, c, k, st)
+        else:
+            status = self.lib.ppyb200_matmul_bf16_kmajor(a.data_ptr(), w.data_ptr(), None,
+                                                         x.data_ptr(), tokens, c, k)
+        self._check(status, what)
+        if self.shard.size > 1:
+            dist.all_reduce(x, group=self.group)
+
+    def forward(self, ids, logits=None):
+        """This rank's logits [batch, length, v1 - v0] (f32) for the vocab rows [v0, v1)."""
+        import torch
+
+        cfg = self.config
+        batch, length = ids.shape
+        tokens = batch * length
+        c = cfg.width
+        hl = self.shard.heads[1] - self.shard.heads[0]
+        wl = hl * cfg.head_dim
+        fl = self.shard.hidden[1] - self.shard.hidden[0]
+        v0, v1 = self.shard.vocab
+        if length > cfg.context or length % 128 != 0:
+            raise runtime.B200Error("the sequence length is a multiple of 128 up to the context")
+        ids = ids.contiguous()
+        s = self._scratch(tokens)
+        x, h, qkv, vt, att, f = s["x"], s["h"], s["qkv"], s["vt"], s["att"], s["f"]
+        status = s["status"]
+        if logits is None:
+            logits = torch.empty(batch, length, v1 - v0, dtype=torch.float32, device="cuda")
+        lib = self.lib
+        st = status.data_ptr()
+        status.zero_()
+        self._check(lib.ppyb200_gpt2_embed(ids.data_ptr(), self.wte.data_ptr(),
+                                           self.wpe.data_ptr(), x.data_ptr(), tokens, length, c,
+                                           cfg.vocab, st), "embed")
+        ln = self.layernorm.device.layernorm_bf16
+        for blk in self.blocks:
+            self._check(ln(x, blk["ln1_g"], blk["ln1_b"], h).status, "layernorm")
+            self._check(lib.ppyb200_linear_qkv_bf16(h.data_ptr(), blk["w_qkv"].data_ptr(),
+                                                    blk["b_qkv"].data_ptr(), qkv.data_ptr(),
+                                                    vt.data_ptr(), tokens, c, length, hl, st),
+                        "qkv")
+            self._check(lib.ppyb200_attention_causal_vt_bf16(qkv.data_ptr(), vt.data_ptr(),
+                                                             att.data_ptr(), batch, length, hl,
+                                                             cfg.head_dim, st), "attention")
+            self._row_parallel(att, blk["w_o"], blk["b_o"], x, tokens, wl, st, "out projection")
+            self._check(ln(x, blk["ln2_g"], blk["ln2_b"], h).status, "layernorm")
+            self._check(lib.ppyb200_linear_bf16(h.data_ptr(), blk["w_fc"].data_ptr(),
+                                                blk["b_fc"].data_ptr(), f.data_ptr(), tokens, fl,
+                                                c, 1, st), "fc")
+            self._row_parallel(f, blk["w_proj"], blk["b_proj"], x, tokens, fl, st, "proj")
+        self._check(ln(x, self.lnf_g, self.lnf_b, h).status, "layernorm")
+        self._check(lib.ppyb200_matmul_bf16_kmajor(h.data_ptr(), self.head.data_ptr(), None,
+                                                   logits.data_ptr(), tokens, v1 - v0, c),
+                    "lm head")
+        return logits
+
+    def status(self) -> int:
+        for buffers in self._buffers.values():
+            return int(buffers["status"].item())
+        return 0

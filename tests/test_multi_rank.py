@@ -87,3 +87,97 @@ def test_reference_arm_under_torchrun_prints_one_line():
     record = json.loads(lines[0])
     assert record["impl"] == "reference" and record["value"] > 0
     assert record["cpu_baseline"]["kind"] == "port"
+
+
+# ---------------------------------------------------------------- GPT-2 tensor parallel
+
+def _tp_block_rank(rank: int, world: int, port: int, queue) -> None:
+    """One block of the TP forward in float32 torch on a gloo rank, with the weights this rank
+    holds (ppy_b200.gpt2_tp.shard_block) and the reduction the GPU path makes: rank 0 adds
+    its partial product, the bias and the residual, the others their partial product, then an
+    all-reduce (sum)."""
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    sys.path.insert(0, str(REPO))
+    from ppy_b200.gpt2 import Config
+    from ppy_b200.gpt2_tp import shard_block, shard_ranges
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = Config(layers=1, width=256, heads=4, vocab=1000, context=128)
+    c, d, heads = cfg.width, cfg.head_dim, cfg.heads
+    g = torch.Generator().manual_seed(11)
+    blk = {"ln1_g": 1 + 0.1 * torch.randn(c, generator=g), "ln1_b": 0.1 * torch.randn(c, generator=g),
+           "w_qkv": 0.05 * torch.randn(3 * c, c, generator=g), "b_qkv": 0.1 * torch.randn(3 * c, generator=g),
+           "w_o": 0.05 * torch.randn(c, c, generator=g), "b_o": 0.1 * torch.randn(c, generator=g),
+           "ln2_g": 1 + 0.1 * torch.randn(c, generator=g), "ln2_b": 0.1 * torch.randn(c, generator=g),
+           "w_fc": 0.05 * torch.randn(4 * c, c, generator=g), "b_fc": 0.1 * torch.randn(4 * c, generator=g),
+           "w_proj": 0.05 * torch.randn(c, 4 * c, generator=g), "b_proj": 0.1 * torch.randn(c, generator=g)}
+    batch, length = 2, 64
+    x0 = torch.randn(batch, length, c, generator=g)
+
+    def attention(qkv, nh):
+        q, k, v = qkv.split(nh * d, dim=-1)
+        shape = lambda t: t.reshape(batch, length, nh, d).transpose(1, 2)  # noqa: E731
+        a = F.scaled_dot_product_attention(shape(q), shape(k), shape(v), is_causal=True)
+        return a.transpose(1, 2).reshape(batch, length, nh * d)
+
+    # the whole block
+    x = x0.clone()
+    hh = F.layer_norm(x, (c,), blk["ln1_g"], blk["ln1_b"], 1e-5)
+    x = x + F.linear(attention(F.linear(hh, blk["w_qkv"], blk["b_qkv"]), heads), blk["w_o"], blk["b_o"])
+    n = F.layer_norm(x, (c,), blk["ln2_g"], blk["ln2_b"], 1e-5)
+    x = x + F.linear(F.gelu(F.linear(n, blk["w_fc"], blk["b_fc"]), approximate="tanh"),
+                     blk["w_proj"], blk["b_proj"])
+    whole = x
+
+    # this rank's share
+    shard = shard_ranges(cfg, rank, world)
+    mine = shard_block(blk, cfg, shard)
+    nh = shard.heads[1] - shard.heads[0]
+
+    def row_parallel(a, w, b, x):
+        y = x + F.linear(a, w, b) if rank == 0 else F.linear(a, w)
+        dist.all_reduce(y)
+        return y
+
+    x = x0.clone()
+    hh = F.layer_norm(x, (c,), mine["ln1_g"], mine["ln1_b"], 1e-5)
+    x = row_parallel(attention(F.linear(hh, mine["w_qkv"], mine["b_qkv"]), nh), mine["w_o"], mine["b_o"], x)
+    n = F.layer_norm(x, (c,), mine["ln2_g"], mine["ln2_b"], 1e-5)
+    x = row_parallel(F.gelu(F.linear(n, mine["w_fc"], mine["b_fc"]), approximate="tanh"),
+                     mine["w_proj"], mine["b_proj"], x)
+    queue.put((rank, float((x - whole).abs().max()), float(whole.abs().max())))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_block_equals_the_whole_block(world):
+    ctx = torch.multiprocessing.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_block_rank, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    for _ in range(world):
+        rank, err, scale = queue.get(timeout=10)
+        assert err <= 1e-5 * scale, (rank, err, scale)
+
+
+def test_tensor_parallel_shards_tile_the_model():
+    sys.path.insert(0, str(REPO))
+    from ppy_b200.gpt2 import GPT2_124M
+    from ppy_b200.gpt2_tp import shard_ranges
+
+    for size in (1, 2, 4):
+        shards = [shard_ranges(GPT2_124M, r, size) for r in range(size)]
+        for key, total in (("heads", 12), ("hidden", 3072), ("vocab", 50257)):
+            spans = [getattr(s, key) for s in shards]
+            assert spans[0][0] == 0 and spans[-1][1] == total
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    with pytest.raises(ValueError):
+        shard_ranges(GPT2_124M, 0, 8)  # 96-wide slices are not whole 64-wide K steps
