@@ -89,7 +89,8 @@ def test_kmajor_refuses_k_not_a_multiple_of_64(lib):
     assert lib.ppyb200_matmul_bf16_kmajor(_ptr(a), _ptr(bt), None, _ptr(out), 128, 256, 96) == 1
 
 
-@pytest.mark.parametrize("m,n,k", [(100, 70, 64), (1, 50257, 128), (300, 520, 192)])
+@pytest.mark.parametrize("m,n,k", [(100, 70, 64), (1, 50257, 128), (300, 520, 192),
+                                   (200, 50257, 64), (130, 131, 128)])
 def test_tensor_cores_take_ragged_m_and_n(lib, m, n, k):
     """Edge tiles: TMA zero-fills past M and N, the epilogue stores only inside."""
     a, b, bias = _operands(m, n, k, seed=6)
