@@ -238,25 +238,6 @@ struct BiasEpilogue {
   }
 };
 
-// The same four columns at a time, for C rows that start on 16-byte boundaries (ldc % 4 == 0,
-// N % 4 == 0, C and bias 16-byte aligned).
-struct BiasQuadEpilogue {
-  static constexpr bool kQuads = true;
-  const float* bias;
-  float* c;
-  int64_t ldc;
-  __device__ __forceinline__ void store_quads(const float4 (&v)[8], int64_t row, int count,
-                                              int64_t col) const {
-    const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-    float* p = c + row * ldc + col;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < count)
-        __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc),
-               make_float4(v[i].x + b.x, v[i].y + b.y, v[i].z + b.z, v[i].w + b.w));
-  }
-};
 
 template <class Epi>
 __global__ void __launch_bounds__(THREADS, 1)
