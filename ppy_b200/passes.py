@@ -1,0 +1,158 @@
+"""Backend-stage passes of the b200 backend.
+
+`CommonTensorsToBuffers` makes functions written over `ppy.Tensor` parameters (PPy source
+typed by the `b200_tensor` plugin, `ppy_b200.tensor_plugin`) look like the tensor functions of
+a `.ppyir` module, which take buffers and `tensor.load` / `tensor.store` them
+(lower_tensor.py:125-131 of the reference: a tensor crosses a call as a buffer):
+
+    %a: tensor<f32, N>  (a parameter)  ->  %a: buffer<f32>, %x = tensor.load %a
+    b200.assign %out, %v               ->  tensor.store %v, %out      (%out: buffer<f32>)
+    b200.fill %s {dtype}               ->  tensor.fill %s'            (%s' the constant in dtype)
+
+and first forwards the stack slots the frontend gives every local tensor variable
+(`core.alloca` of a tensor, `core.store`, `core.load` in one block) to the values stored, so
+that the tensor operations read one another directly.
+
+The backend's C ABI then passes every such parameter as a pointer and a length, like any
+buffer, and `role` in the manifest says whether the call reads it, writes it or both.
+"""
+
+from __future__ import annotations
+
+from ppy_compiler.ir import BufferType, Builder, PtrType
+from ppy_compiler.ir.dialects import core
+from ppy_compiler.ir.dialects import tensor as tensor_dialect
+from ppy_compiler.ir.passes import Pass, PassContext
+
+from .scalar_c import Unsupported
+
+__all__ = ["CommonTensorsToBuffers", "common_tensors_to_buffers"]
+
+
+def _cast(value, dtype: str):
+    """A constant's value as the element type `dtype` takes it."""
+    if dtype.startswith(("i", "u")):
+        return int(value)
+    return float(value)
+
+
+def common_tensors_to_buffers(module) -> bool:
+    """Rewrite `module` in place; True if anything changed."""
+    changed = False
+    for function in module.functions.values():
+        if function.is_declaration:
+            continue
+        changed |= _slots(function)
+        changed |= _fills(function)
+        changed |= _parameters(function)
+    return changed
+
+
+def _slots(function) -> bool:
+    """Forward `core.store` to `core.load` through tensor stack slots of a one-block function."""
+    blocks = function.body.blocks
+    if len(blocks) != 1:
+        return False
+    slots = set()
+    current: dict[int, object] = {}
+    dead = []
+    changed = False
+    for op in list(blocks[0].operations):
+        if op.name == "core.alloca":
+            t = op.results[0].type
+            if isinstance(t, PtrType) and tensor_dialect.describe(t.pointee) is not None:
+                slots.add(id(op.results[0]))
+                dead.append(op)
+        elif op.name == "core.store" and id(op.operands[1]) in slots:
+            current[id(op.operands[1])] = op.operands[0]
+            op.erase()
+            changed = True
+        elif op.name == "core.load" and id(op.operands[0]) in slots:
+            value = current.get(id(op.operands[0]))
+            if value is None:
+                raise Unsupported(f"@{function.name}: a tensor variable read before it is set")
+            op.results[0].replace_all_uses_with(value)
+            op.erase()
+            changed = True
+    for op in dead:
+        if not op.results[0].uses:
+            op.erase()
+    return changed
+
+
+def _fills(function) -> bool:
+    changed = False
+    for op in list(function.operations()):
+        if op.name != "b200.fill":
+            continue
+        scalar = op.operands[0]
+        result = op.results[0]
+        dtype = tensor_dialect.describe(result.type).dtype
+        b = Builder().before(op)
+        owner = scalar.owner
+        if getattr(owner, "name", None) == "core.const":
+            scalar = core.const(b, _cast(owner.attributes["value"], str(dtype)), dtype)
+        elif scalar.type != dtype:
+            raise Unsupported(f"@{function.name}: bt.full of a {scalar.type} value as {dtype}",
+                              "bt.full of a constant, or of a scalar of the element type")
+        fill = b.create("tensor.fill", (scalar,), (result.type,))
+        result.replace_all_uses_with(fill.results[0])
+        op.erase()
+        changed = True
+    return changed
+
+
+def _parameters(function) -> bool:
+    entry = function.entry
+    if entry is None:
+        return False
+    if any(tensor_dialect.describe(t) is not None for t in function.results):
+        raise Unsupported(f"@{function.name}: a tensor result",
+                          "results written into ppy.Mut[ppy.Tensor] parameters with bt.assign")
+    params = list(function.params)
+    changed = False
+    for index, (name, declared) in enumerate(function.params):
+        info = tensor_dialect.describe(declared)
+        if info is None:
+            continue
+        argument = entry.arguments[index]
+        buffer = BufferType(info.dtype)
+        argument.type = buffer
+        params[index] = (name, buffer)
+        # writes: b200.assign %arg, %v  ->  tensor.store %v, %arg (the value broadcast first)
+        for user, slot in list(argument.uses):
+            if getattr(user, "name", None) == "b200.assign" and slot == 0:
+                value = user.operands[1]
+                b = Builder().before(user)
+                if tuple(tensor_dialect.describe(value.type).shape) != tuple(info.shape):
+                    value = b.create("tensor.broadcast", (value,), (declared,)).results[0]
+                b.create("tensor.store", (value, argument), ())
+                user.erase()
+        # reads: one load at the top of the function (the stores just made keep the buffer)
+        reads = [(user, slot) for user, slot in argument.uses
+                 if not (getattr(user, "name", None) == "tensor.store" and slot == 1)]
+        if reads:
+            first = entry.operations[0] if entry.operations else None
+            b = Builder(entry) if first is None else Builder().before(first)
+            load = b.create("tensor.load", (argument,), (declared,), result_names=(name,))
+            loaded = load.results[0]
+            for user, slot in reads:
+                user.set_operand(slot, loaded)
+        changed = True
+    if changed:
+        function.params = tuple(params)
+        for attributes in function.param_attributes:
+            attributes.pop("ppy.kind", None)
+    return changed
+
+
+class CommonTensorsToBuffers(Pass):
+    """Backend-stage pass: tensor parameters become buffers (see the module docstring)."""
+
+    name = "b200-common-tensors-to-buffers"
+
+    def run(self, module, ctx: PassContext) -> bool:
+        changed = common_tensors_to_buffers(module)
+        if changed:
+            ctx.invalidate()
+        return changed

@@ -69,6 +69,30 @@ def test_gelu_full_size_against_the_oracle(rt):
     assert np.array_equal(tout.cpu().numpy(), out)
 
 
+def test_gelu_from_ppy_source_matches_the_ir_module(rt):
+    """tests/golden/gelu_source.ppy (PPy source over ppy.Tensor, typed by the b200_tensor
+    plugin) builds the same kernel as the .ppyir fixture: the same bits, host and device."""
+    module = _load(rt, "gelu_source")
+    ir_module = _load(rt, "gelu")
+    rng = np.random.default_rng(3)
+    n = 1 << 20  # the shape the source declares
+    a, b, c = (rng.uniform(-4, 4, n).astype(np.float32) for _ in range(3))
+    out = np.empty_like(a)
+    assert module.gelu_source_gelu_chain(a, b, c, out).status == 0
+    within(out, oracle.gelu_chain(a, b, c))
+    same = np.empty_like(a)
+    assert ir_module.gelu_chain(a, b, c, same).status == 0
+    assert np.array_equal(out, same)
+    ta, tb, tc = (torch.from_numpy(x).cuda() for x in (a, b, c))
+    tout = torch.empty_like(ta)
+    assert module.device.gelu_source_gelu_chain(ta, tb, tc, tout).status == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(tout.cpu().numpy(), out)
+    # a buffer of another length than the declared shape takes the fallback
+    short = np.empty(n - 1, np.float32)
+    assert module.gelu_source_gelu_chain(a[:-1], b[:-1], c[:-1], short).status == 1
+
+
 def test_gelu_unaligned_and_ragged_device_buffers(rt):
     module = _load(rt, "gelu")
     rng = np.random.default_rng(5)
