@@ -253,6 +253,12 @@ class _FunctionEmitter:
             if fn in ("ndtr", "logit"):
                 fn = "ppyb200::" + fn
             return [f"{r} = {fn}({self.v(op.operands[0])});"]
+        if dialect == "concurrency":
+            # parallel.range already split into host-thread chunks (LowerParallel's threads
+            # route, lower_parallel.py:141-318): the GPU wants the whole range
+            raise Unsupported(f"{name}: ppy.parallel.range lowered to host threads",
+                              "parallel.reduce/for/map as the IR op: set `[tool.ppy.parallel] "
+                              "backend = \"openmp\"` in pyproject.toml")
         if dialect != "core":
             raise Unsupported(f"{name}", "core, math, special and parallel operations")
         a = op.attributes

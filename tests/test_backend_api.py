@@ -152,3 +152,46 @@ def test_committed_prebuilt_modules_are_what_the_backend_generates(ppy_compiler,
         written = artifacts.write_module(module, tmp_path / name, compile_library=False)
         for path in written:
             assert path.read_text() == (directory / path.name).read_text(), path.name
+
+
+COLLATZ_SOURCE = textwrap.dedent("""
+    import ppy
+
+
+    def collatz_steps(n: int) -> int:
+        steps = 0
+        while n != 1:
+            if n % 2 == 0:
+                n = n // 2
+            else:
+                n = 3 * n + 1
+            steps += 1
+        return steps
+
+
+    def collatz_sum(lo: int, hi: int) -> int:
+        total = 0
+        for i in ppy.parallel.range(lo, hi):
+            total += collatz_steps(i)
+        return total
+""")
+
+
+def test_parallel_range_source_needs_the_ir_op_and_says_how(project):
+    """PPy source with ppy.parallel.range (examples/35_parallel_range): under the default
+    threads route the range arrives already split into host-thread chunks, which the backend
+    refuses naming the setting that keeps it whole; with that setting it builds a reduce
+    kernel."""
+    root, site = project
+    (root / "collatz.ppy").write_text(COLLATZ_SOURCE)
+    done = _ppy(root, site, "build", "collatz.ppy", "--backend", "b200", "-o", "out")
+    assert done.returncode != 0
+    text = done.stdout + done.stderr
+    assert "E1802" in text and '[tool.ppy.parallel] backend = "openmp"' in text
+    with (root / "pyproject.toml").open("a") as f:
+        f.write('\n[tool.ppy.parallel]\nbackend = "openmp"\n')
+    done = _ppy(root, site, "build", "collatz.ppy", "--backend", "b200", "-o", "out")
+    assert done.returncode == 0, done.stdout + done.stderr
+    manifest = json.loads((root / "out" / "collatz.json").read_text())
+    kernels = {fn["name"]: fn["kernels"] for fn in manifest["functions"]}
+    assert kernels["collatz_collatz_sum"] == ["reduce"]
