@@ -24,6 +24,7 @@ MAP_MIN_BLOCKS = 0
 ROW_MIN_BLOCKS = 0
 #: Shared memory a pipelined row kernel may take per block (two row buffers per warp).
 ROW_SMEM_LIMIT = 100 * 1024
+ROW_STAGES = 3  # rows a warp has in flight: the one it computes and ROW_STAGES - 1 prefetched
 #: Threads of a row kernel block when a row takes at most one warp.
 ROW_THREADS = 256
 
@@ -532,7 +533,10 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
         seg[i] = buf_bytes
         buf_bytes += rpw * kernel.cols * P.size_of(kernel.inputs[i].dtype)
         buf_bytes = (buf_bytes + 15) // 16 * 16
-    smem_bytes = warps * 2 * buf_bytes
+    stages = ROW_STAGES
+    while stages > 2 and warps * stages * buf_bytes > ROW_SMEM_LIMIT:
+        stages -= 1
+    smem_bytes = warps * stages * buf_bytes
     if smem_bytes > ROW_SMEM_LIMIT:
         pipelined = False
     bounds = f"{block}, {ROW_MIN_BLOCKS}" if ROW_MIN_BLOCKS else f"{block}"
@@ -659,6 +663,12 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
                 B.append(f"const {ct} {s.var} = {expr};")
             continue
         # elem and cols statements: one value per element of this lane's chunks
+        f32_row_divide = (s.op == "div" and _compute_dtype(s.dtype) == "f32"
+                          and cls[s.args[1]] in ("rows", "scalar"))
+        if f32_row_divide:
+            # an f32 division by one value per row: its reciprocal once per row, then a
+            # multiply per element (within an ulp and a half of the division)
+            B.append(f"const {ct} {s.var}_rcp = {ct}(1) / {s.args[1]};")
         B.append(f"{ct} {s.var}[NCH][VEC];")
         B.append("#pragma unroll")
         B.append("for (int j = 0; j < NCH; ++j) {")
@@ -666,6 +676,12 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
         B.append("  for (int u = 0; u < VEC; ++u) {")
         if s.op == "input":
             B.append(f"    {s.var}[j][u] = {input_expr(s, 'elem')};")
+        elif f32_row_divide:
+            B.append(f"    {s.var}[j][u] = {value(s.args[0], 'elem')} * {s.var}_rcp;")
+        elif s.op == "math" and s.attrs["fn"] == "exp" and _compute_dtype(s.dtype) == "f32":
+            # the SFU exponential (PTX ex2.approx after a scale by log2 e; CUDA's __expf):
+            # within 2 + 1.16 |x| ulp, inside the f32 tolerance
+            B.append(f"    {s.var}[j][u] = __expf({value(s.args[0], 'elem')});")
         else:
             expr, pre = stmt_expr(s, lambda v: value(v, "elem"), dtypes)
             B.extend("    " + p for p in pre)
@@ -697,7 +713,8 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
         L.append("  const int64_t groups = (R + RPW - 1) / RPW;")
         L.append("  const int64_t first = (int64_t)blockIdx.x * WPB + warp;")
         L.append("  const int64_t stride = (int64_t)gridDim.x * WPB;")
-        L.append("  unsigned char* wbuf = smem + warp * 2 * BUF;")
+        L.append(f"  constexpr int STAGES = {stages};")
+        L.append("  unsigned char* wbuf = smem + warp * STAGES * BUF;")
         # prefetch of one row group into buffer b: every lane copies the chunks it reads
         P_ = ["  auto prefetch = [&](int64_t g, int b) {",
               "    const int64_t prow = g * RPW + slot;",
@@ -714,13 +731,19 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
             P_.append("    }")
         P_.append("  };")
         L.extend(P_)
-        L.append("  if (first < groups) prefetch(first, 0);")
-        L.append("  ppyb200::cp_async_commit();")
-        L.append("  int b = 0;")
-        L.append("  for (int64_t g = first; g < groups; g += stride, b ^= 1) {")
-        L.append("    if (g + stride < groups) prefetch(g + stride, b ^ 1);")
+        # STAGES - 1 row groups in flight ahead of the one computed; one commit group per
+        # prefetch (empty past the end), so that wait<STAGES - 1> always means "this one"
+        L.append("  #pragma unroll")
+        L.append("  for (int k = 0; k < STAGES - 1; ++k) {")
+        L.append("    if (first + k * stride < groups) prefetch(first + k * stride, k);")
         L.append("    ppyb200::cp_async_commit();")
-        L.append("    ppyb200::cp_async_wait<1>();")
+        L.append("  }")
+        L.append("  int b = 0;")
+        L.append("  for (int64_t g = first; g < groups; g += stride, b = (b + 1) % STAGES) {")
+        L.append("    const int64_t ahead = g + (STAGES - 1) * stride;")
+        L.append("    if (ahead < groups) prefetch(ahead, (b + STAGES - 1) % STAGES);")
+        L.append("    ppyb200::cp_async_commit();")
+        L.append("    ppyb200::cp_async_wait<STAGES - 1>();")
         L.append("    const unsigned char* buf = wbuf + b * BUF;")
         L.append("    const int64_t row = g * RPW + slot;")
         L.append("    const bool active = row < R;")
