@@ -103,6 +103,23 @@ def test_tensor_cores_take_ragged_m_and_n(lib, m, n, k):
     assert torch.all(out[m] == 7.0)
 
 
+@pytest.mark.parametrize("offset", [4, 36, 1])
+def test_logit_rows_at_any_offset(lib, offset):
+    """C inside a larger buffer, rows of 50257 floats starting 16-byte aligned (offsets 4 and
+    36 floats, not on a 128-byte line) or only 4-byte aligned (offset 1): every element of C
+    lands once and nothing either side of it is touched."""
+    m, n, k = 260, 50257, 128
+    a, b, bias = _operands(m, n, k, seed=7)
+    da, dbt, dbias = a.cuda(), b.t().contiguous().cuda(), bias.cuda()
+    buf = torch.full((offset + m * n + 64,), 7.0, device="cuda")
+    out = buf[offset:offset + m * n].view(m, n)
+    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(da), _ptr(dbt), _ptr(dbias), _ptr(out), m, n,
+                                          k) == 0
+    torch.cuda.synchronize()
+    _check(out, _reference(a, b, bias), rel=1e-4)
+    assert torch.all(buf[:offset] == 7.0) and torch.all(buf[offset + m * n:] == 7.0)
+
+
 @pytest.mark.parametrize("m,n,k", [(100, 70, 33), (1, 256, 64), (129, 257, 65)])
 def test_ragged_shapes_run_on_cuda_cores(lib, m, n, k):
     a, b, bias = _operands(m, n, k, seed=2)
