@@ -54,6 +54,8 @@ def _args():
     p.add_argument("--workload", default="gelu",
                    choices=["gelu", "rows", "collatz", "gemm", "gpt2", "gpt2_tp"])
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--tp", type=int, default=0,
+                   help="gpt2_tp: ranks per tensor-parallel group (0: the widest that fits)")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU-baseline sample length (seconds of host work)")
     return p.parse_args()
@@ -514,39 +516,54 @@ class Gpt2(Workload):
 
 
 class Gpt2TP(Gpt2):
-    """The tensor-parallel variant: every rank works on the whole batch with 12/N heads,
-    3072/N hidden units and 50257/N logits columns; two all-reduces of the residual stream
-    per block (N in {1, 2, 4})."""
+    """The tensor-parallel variant: the ranks of a group work on the group's sequences with
+    12/T heads, 3072/T hidden units and 50257/T logits columns each, two all-reduces of the
+    residual stream per block (T in {1, 2, 4}); N ranks form N/T such groups, each with its
+    share of the batch (8 GPUs: 2 groups of 4). `--tp` picks T, 0 the widest that fits."""
 
     metric = "GPT-2-124M forward tokens/s, tensor parallel: batch 32 x 1024, logits out"
     kernel = "gpt2_tp_forward"
+    tp = 0
 
     def inputs(self):
         import torch
 
+        from ppy_b200 import gpt2, gpt2_tp
+
+        self.dp, self.tp = gpt2_tp.hybrid_layout(self.dist.world, gpt2.GPT2_124M, self.tp)
+        start, stop = shard_batch(self.BATCH, self.dp, self.dist.rank // self.tp)
         g = torch.Generator().manual_seed(0)
-        self.ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
+        ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
+        self.ids = ids[start:stop].contiguous()
 
     def config(self):
         cfg = super().config()
-        cfg.update(workload="gpt2_124m_forward_tp", parallelism=f"tp{self.dist.world}",
-                   exchange="2 NCCL all-reduces (sum, f32 [32768, 768]) per block")
+        tokens = self.ids.numel()
+        cfg.update(workload="gpt2_124m_forward_tp",
+                   parallelism=f"tp{self.tp}" if self.dp == 1 else f"dp{self.dp}xtp{self.tp}",
+                   exchange=f"2 NCCL all-reduces (sum, f32 [{tokens}, 768]) per block inside "
+                            f"each group of {self.tp}")
         return cfg
 
     def setup_device(self, runtime, torch):
         from ppy_b200 import gpt2, gpt2_tp
 
-        self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0)
+        group = None
+        if self.dist.world > 1:
+            group, _ = gpt2_tp.hybrid_groups(self.tp)
+        self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0, group=group)
         self.gpt2 = gpt2
         self.dids = self.ids.cuda()
         self.pids = self.ids.pin_memory()
         v0, v1 = self.model.shard.vocab
-        self.logits = torch.empty(self.BATCH, self.LENGTH, v1 - v0, device="cuda")
-        self.last = torch.empty(self.BATCH, v1 - v0).pin_memory()
+        b = self.ids.shape[0]
+        self.logits = torch.empty(b, self.LENGTH, v1 - v0, device="cuda")
+        self.last = torch.empty(b, v1 - v0).pin_memory()
 
     def h2d_d2h(self):
         v0, v1 = self.model.shard.vocab
-        return 8 * self.BATCH * self.LENGTH, 4 * self.BATCH * (v1 - v0)
+        b = self.ids.shape[0]
+        return 8 * b * self.LENGTH, 4 * b * (v1 - v0)
 
     def check(self, oracle):
         import torch
@@ -687,6 +704,7 @@ def run_b200(args, dist: Dist) -> None:
     torch.cuda.set_stream(stream)
     runtime.set_stream(stream)
     w = WORKLOADS[args.workload](dist)
+    w.tp = args.tp
     w.inputs()
     w.setup_device(runtime, torch)
     clocks = Clocks(dist.local)
@@ -735,7 +753,7 @@ def run_b200(args, dist: Dist) -> None:
         sums = dist.sum_i64([w.sum])
         units_all = float(sums[0])
     if isinstance(w, Gpt2TP):
-        units_all = float(units)  # every rank works on the same tokens
+        units_all = float(units) * w.dp  # the ranks of a group share their tokens
     elif isinstance(w, Gpt2):
         units_all = float(dist.sum_i64([int(units)])[0])
     value = to_metric(w, units_all * args.steps, total_ms / 1e3)

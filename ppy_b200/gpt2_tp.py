@@ -16,7 +16,9 @@ LM head:
     LM head          vocab-parallel: this rank's slice of the logits
 
 Two all-reduces of the f32 residual stream [tokens, 768] per block. g divides 12 and the local
-widths (768/g and 3072/g) stay multiples of 64 (the tensor-core K step): g in {1, 2, 4}.
+widths (768/g and 3072/g) stay multiples of 64 (the tensor-core K step): g in {1, 2, 4}. More
+ranks than that run as data-parallel groups of tensor-parallel ranks (`hybrid_layout`,
+`hybrid_groups`): 8 GPUs as 2 groups of 4, each group with half the batch.
 """
 
 from __future__ import annotations
@@ -26,7 +28,8 @@ from dataclasses import dataclass
 from . import runtime
 from .gpt2 import GPT2, GPT2_124M, Config, _bind
 
-__all__ = ["TPShard", "shard_ranges", "shard_block", "GPT2TensorParallel"]
+__all__ = ["TPShard", "splits", "shard_ranges", "hybrid_layout", "hybrid_groups", "shard_block",
+           "GPT2TensorParallel"]
 
 
 @dataclass(frozen=True)
@@ -40,10 +43,16 @@ class TPShard:
     vocab: tuple[int, int]   # [first, last) LM head row
 
 
+def splits(config: Config, size: int) -> bool:
+    """Whether `size` ranks split the heads, and the widths into whole 64-wide K steps."""
+    return (size >= 1 and config.heads % size == 0 and config.width % size == 0
+            and (config.width // size) % 64 == 0 and (4 * config.width // size) % 64 == 0)
+
+
 def shard_ranges(config: Config, rank: int, size: int) -> TPShard:
     if size < 1 or not 0 <= rank < size:
         raise ValueError(f"rank {rank} of {size}")
-    if config.heads % size or (config.width // size) % 64 or (4 * config.width // size) % 64:
+    if not splits(config, size):
         raise ValueError(f"{size} ranks do not split {config.heads} heads and the widths "
                          f"into 64-wide slices")
     hl = config.heads // size
@@ -52,6 +61,40 @@ def shard_ranges(config: Config, rank: int, size: int) -> TPShard:
     v0 = rank * per + min(rank, extra)
     return TPShard(rank, size, (rank * hl, (rank + 1) * hl), (rank * fl, (rank + 1) * fl),
                    (v0, v0 + per + (1 if rank < extra else 0)))
+
+
+def hybrid_layout(world: int, config: Config = GPT2_124M, tp: int = 0) -> tuple[int, int]:
+    """(dp, tp): `world` ranks as dp = world / tp groups of tp consecutive ranks, each group
+    tensor-parallel over its share of the batch. tp = 0 takes the widest split that
+    `shard_ranges` accepts and that divides `world` (GPT-2-124M on 8 ranks: 2 groups of 4)."""
+    if world < 1:
+        raise ValueError(f"{world} ranks")
+    if tp:
+        if world % tp or not splits(config, tp):
+            raise ValueError(f"{world} ranks do not form groups of {tp} tensor-parallel ranks")
+        return world // tp, tp
+    best = max(t for t in range(1, world + 1) if world % t == 0 and splits(config, t))
+    return world // best, best
+
+
+def hybrid_groups(tp: int):
+    """(group, dp_index): this rank's tensor-parallel group -- ranks [i * tp, (i + 1) * tp) form
+    group i -- and i. Every rank creates every group, in the same order, as
+    torch.distributed.new_group requires; with tp equal to the world the group is the world."""
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if world % tp:
+        raise ValueError(f"{world} ranks do not form groups of {tp}")
+    if tp == world:
+        return dist.group.WORLD, 0
+    mine = None
+    for i in range(world // tp):
+        ranks = list(range(i * tp, (i + 1) * tp))
+        group = dist.new_group(ranks)
+        if rank in ranks:
+            mine = group
+    return mine, rank // tp
 
 
 def shard_block(blk: dict, config: Config, shard: TPShard) -> dict:

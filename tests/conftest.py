@@ -40,8 +40,8 @@ def ppy_compiler():
 
 def within(actual, expected, rel: float = 1e-5, floor: float = 1.0):
     """|actual - expected| <= rel * max(|expected|, floor), NaN where expected is NaN,
-    equal infinities: the fp32 tolerance of the north star, written with a floor so that
-    it stays meaningful where the reference is near zero."""
+    equal infinities: the 1e-5 relative fp32 tolerance, written with a floor so that it
+    stays meaningful where the reference is near zero."""
     import numpy as np
 
     actual = np.asarray(actual, np.float64)

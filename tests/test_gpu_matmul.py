@@ -1,7 +1,7 @@
 """The matmul entry points through the C ABI, against a float64 evaluation of the same
-bf16 inputs (NumPy has no bf16; torch rounds them). Tolerance for the bf16 paths: the
-north star's 2e-2 relative on outputs, written here as |C - ref| <= 2e-2 * max(|ref|,
-rms(ref)); the tensor-core kernel accumulates in f32 and lands far inside it."""
+bf16 inputs (NumPy has no bf16; torch rounds them). Tolerance for the bf16 paths: 2e-2
+relative on outputs, written here as |C - ref| <= 2e-2 * max(|ref|, rms(ref)); the
+tensor-core kernel accumulates in f32 and lands far inside it."""
 
 from __future__ import annotations
 

@@ -1,7 +1,8 @@
-"""The tensor-parallel GPT-2 forward (ppy_b200.gpt2_tp) on 2 GPUs, one process each over NCCL:
-every rank's logits slice against the torch float32 forward of the same weights (the
+"""The tensor-parallel GPT-2 forward (ppy_b200.gpt2_tp) on 2, 4 and 8 GPUs, one process each over
+NCCL -- one group of 2, two data-parallel groups of 2, two groups of 4: every rank's logits
+slice of its group's sequences against the torch float32 forward of the same weights (the
 reference's ATen block, examples/46_gpt2/gpt2.ppy:18-57) and against the one-GPU forward of
-the b200 kernels. Skipped on a box with fewer than 2 GPUs."""
+the b200 kernels. Each case is skipped on a box with fewer GPUs."""
 
 from __future__ import annotations
 
@@ -24,7 +25,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank: int, world: int, port: int, queue) -> None:
+def _rank(rank: int, world: int, port: int, queue, tp: int = 0) -> None:
     import datetime
 
     import torch.distributed as dist
@@ -40,9 +41,12 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
         runtime.init(rank)
         runtime.set_stream(torch.cuda.current_stream())
         cfg = gpt2.Config(layers=2)
-        tp = gpt2_tp.GPT2TensorParallel(cfg, seed=0)
+        dp, tp_size = gpt2_tp.hybrid_layout(world, cfg, tp)
+        group, dpi = gpt2_tp.hybrid_groups(tp_size)
+        tp = gpt2_tp.GPT2TensorParallel(cfg, seed=0, group=group)
         g = torch.Generator(device="cuda").manual_seed(5)
-        ids = torch.randint(0, 50257, (2, 256), device="cuda", generator=g)
+        ids = torch.randint(0, 50257, (2 * dp, 256), device="cuda", generator=g)
+        ids = ids[2 * dpi:2 * dpi + 2].contiguous()  # this group's sequences
         got = tp.forward(ids)
         torch.cuda.synchronize()
         status = tp.status()
@@ -59,24 +63,25 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_forward_on_two_gpus():
+@pytest.mark.parametrize("world,tp", [(2, 0), (4, 2), (8, 0)])
+def test_tensor_parallel_forward(world, tp):
     if not torch.cuda.is_available():
         pytest.fail("a GPU test ran without a CUDA device")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = torch.multiprocessing.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, queue, tp)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    for _ in range(2):
+    for _ in range(world):
         rank, status, worst, norm, vs_one = queue.get(timeout=10)
         assert status == 0, rank
-        # logits, tensor-relative (the north star's 2e-2 for the bf16 GEMM paths)
+        # logits, tensor-relative (2e-2, the bf16 GEMM paths' tolerance)
         assert worst <= 2e-2 and norm <= 2e-2, (rank, worst, norm)
         # against one GPU: the same kernels, partial products summed in another order
         assert vs_one <= 1e-2, (rank, vs_one)

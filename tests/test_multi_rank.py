@@ -91,17 +91,18 @@ def test_reference_arm_under_torchrun_prints_one_line():
 
 # ---------------------------------------------------------------- GPT-2 tensor parallel
 
-def _tp_block_rank(rank: int, world: int, port: int, queue) -> None:
+def _tp_block_rank(rank: int, world: int, port: int, queue, tp: int = 0) -> None:
     """One block of the TP forward in float32 torch on a gloo rank, with the weights this rank
-    holds (ppy_b200.gpt2_tp.shard_block) and the reduction the GPU path makes: rank 0 adds
-    its partial product, the bias and the residual, the others their partial product, then an
-    all-reduce (sum)."""
+    holds (ppy_b200.gpt2_tp.shard_block) and the reduction the GPU path makes: rank 0 of the
+    group adds its partial product, the bias and the residual, the others their partial
+    product, then an all-reduce (sum) over the group. With tp < world the ranks form groups
+    of tp (ppy_b200.gpt2_tp.hybrid_groups), each with its share of the batch."""
     import torch.distributed as dist
     import torch.nn.functional as F
 
     sys.path.insert(0, str(REPO))
     from ppy_b200.gpt2 import Config
-    from ppy_b200.gpt2_tp import shard_block, shard_ranges
+    from ppy_b200.gpt2_tp import hybrid_groups, hybrid_layout, shard_block, shard_ranges
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -114,8 +115,10 @@ def _tp_block_rank(rank: int, world: int, port: int, queue) -> None:
            "ln2_g": 1 + 0.1 * torch.randn(c, generator=g), "ln2_b": 0.1 * torch.randn(c, generator=g),
            "w_fc": 0.05 * torch.randn(4 * c, c, generator=g), "b_fc": 0.1 * torch.randn(4 * c, generator=g),
            "w_proj": 0.05 * torch.randn(c, 4 * c, generator=g), "b_proj": 0.1 * torch.randn(c, generator=g)}
-    batch, length = 2, 64
-    x0 = torch.randn(batch, length, c, generator=g)
+    dp, tp = hybrid_layout(world, cfg, tp)
+    group, dpi = hybrid_groups(tp)
+    batch, length = 4 // dp, 64
+    x0 = torch.randn(4, length, c, generator=g)[dpi * batch:(dpi + 1) * batch]
 
     def attention(qkv, nh):
         q, k, v = qkv.split(nh * d, dim=-1)
@@ -133,13 +136,14 @@ def _tp_block_rank(rank: int, world: int, port: int, queue) -> None:
     whole = x
 
     # this rank's share
-    shard = shard_ranges(cfg, rank, world)
+    shard = shard_ranges(cfg, dist.get_rank(group), tp)
+    assert shard.rank == rank % tp
     mine = shard_block(blk, cfg, shard)
     nh = shard.heads[1] - shard.heads[0]
 
     def row_parallel(a, w, b, x):
-        y = x + F.linear(a, w, b) if rank == 0 else F.linear(a, w)
-        dist.all_reduce(y)
+        y = x + F.linear(a, w, b) if shard.rank == 0 else F.linear(a, w)
+        dist.all_reduce(y, group=group)
         return y
 
     x = x0.clone()
@@ -152,12 +156,15 @@ def _tp_block_rank(rank: int, world: int, port: int, queue) -> None:
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_tensor_parallel_block_equals_the_whole_block(world):
+@pytest.mark.parametrize("world,tp", [(2, 0), (4, 0), (4, 2)])
+def test_tensor_parallel_block_equals_the_whole_block(world, tp):
+    """Whole tensor-parallel groups, and 4 ranks as 2 data-parallel groups of 2 (the layout 8
+    GPUs take as 2 groups of 4)."""
     ctx = torch.multiprocessing.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_block_rank, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_block_rank, args=(r, world, port, queue, tp))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -181,3 +188,17 @@ def test_tensor_parallel_shards_tile_the_model():
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
     with pytest.raises(ValueError):
         shard_ranges(GPT2_124M, 0, 8)  # 96-wide slices are not whole 64-wide K steps
+
+
+def test_hybrid_layouts():
+    sys.path.insert(0, str(REPO))
+    from ppy_b200.gpt2 import GPT2_124M
+    from ppy_b200.gpt2_tp import hybrid_layout
+
+    assert [hybrid_layout(w, GPT2_124M) for w in (1, 2, 4, 8)] == [(1, 1), (1, 2), (1, 4), (2, 4)]
+    assert hybrid_layout(8, GPT2_124M, tp=2) == (4, 2)
+    assert hybrid_layout(6, GPT2_124M) == (1, 6)  # 2 heads and 128-wide slices per rank
+    assert hybrid_layout(16, GPT2_124M) == (4, 4)
+    for world, tp in ((8, 8), (6, 4), (4, 3)):
+        with pytest.raises(ValueError):
+            hybrid_layout(world, GPT2_124M, tp)
