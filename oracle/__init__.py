@@ -147,3 +147,67 @@ def fold(values: np.ndarray, kind: str, axis: int, dtype) -> np.ndarray:
         else:
             acc = ext_min(acc, item)
     return acc
+
+
+# -- views and copies (lower_tensor.py:695-754) -----------------------------------------------
+
+
+def strided(buffer: np.ndarray, shape: tuple, offset: int, strides: tuple) -> np.ndarray:
+    """The reference's `_View` (lower_tensor.py:695-714): element (i0, i1, ...) of the view is
+    buffer[offset + i0 * strides[0] + i1 * strides[1] + ...] of the flat `buffer`."""
+    flat = np.ascontiguousarray(buffer).ravel()
+    index = np.full(shape, offset, np.int64)
+    for axis, (extent, stride) in enumerate(zip(shape, strides)):
+        step = np.arange(extent, dtype=np.int64) * stride
+        index += step.reshape((1,) * axis + (extent,) + (1,) * (len(shape) - axis - 1))
+    return flat[index]
+
+
+def _row_major(shape: tuple) -> tuple:
+    strides, running = [1] * len(shape), 1
+    for axis in reversed(range(len(shape))):
+        strides[axis] = running
+        running *= shape[axis]
+    return tuple(strides)
+
+
+def transpose(x: np.ndarray, perm: tuple) -> np.ndarray:
+    """`op_transpose` (lower_tensor.py:695-702): the same memory, strides permuted."""
+    strides = _row_major(x.shape)
+    return strided(x, tuple(x.shape[p] for p in perm), 0, tuple(strides[p] for p in perm))
+
+
+def slice_(x: np.ndarray, starts: tuple, stops: tuple, steps: tuple) -> np.ndarray:
+    """`op_slice` (lower_tensor.py:704-714): offset += start * stride, stride *= step, and
+    ceil((stop - start) / step) elements per axis (ir/shape.py:247-261)."""
+    strides = _row_major(x.shape)
+    offset = sum(start * stride for start, stride in zip(starts, strides))
+    shape = tuple(-(-(stop - start) // step) for start, stop, step in zip(starts, stops, steps))
+    return strided(x, shape, offset, tuple(s * k for s, k in zip(strides, steps)))
+
+
+def concat(parts: list, axis: int) -> np.ndarray:
+    """`op_concat` (lower_tensor.py:716-730): each part copied in at its position along axis."""
+    shape = list(parts[0].shape)
+    shape[axis] = sum(p.shape[axis] for p in parts)
+    out = np.empty(shape, parts[0].dtype)
+    position = 0
+    for part in parts:
+        index = [slice(None)] * len(shape)
+        index[axis] = slice(position, position + part.shape[axis])
+        out[tuple(index)] = part
+        position += part.shape[axis]
+    return out
+
+
+def fold_axes(values: np.ndarray, kind: str, axes: tuple, keepdims: bool, dtype) -> np.ndarray:
+    """`op_reduce` over any axes (lower_tensor.py:733-754): every output element folds its
+    elements from the identity in the row-major order of the reduced axes."""
+    values = np.asarray(values, dtype)
+    kept = [d for d in range(values.ndim) if d not in axes]
+    moved = np.transpose(values, tuple(sorted(axes)) + tuple(kept))
+    flat = moved.reshape((-1,) + tuple(values.shape[d] for d in kept))
+    out = fold(flat, kind, 0, dtype)
+    if keepdims:
+        out = out.reshape(tuple(1 if d in axes else values.shape[d] for d in range(values.ndim)))
+    return out

@@ -29,7 +29,7 @@ from ppy_compiler.backend import (
 from ppy_compiler.ir.passes import Pass, PassContext
 
 from . import __version__, artifacts
-from .passes import CommonTensorsToBuffers
+from .passes import CommonTensorsToBuffers, ReductionsToTrailingAxes
 from .scalar_c import Unsupported
 from .toolchain import ARCH, CSRC, nvcc, nvcc_version
 
@@ -86,6 +86,7 @@ class B200Backend(Backend):
 
     def register_passes(self, passes: BackendPassRegistrar) -> None:
         passes.add(CommonTensorsToBuffers)
+        passes.add(ReductionsToTrailingAxes)
         passes.add(KernelPlanRemarks)
 
     def validate(self, module, context: BackendContext) -> None:

@@ -215,8 +215,82 @@ def _program_lines(program: list, value_of, dtypes: dict, indent: str,
     return lines
 
 
+def _strided_map_kernel(kernel: P.MapKernel, fn: P.TensorFunction, src: _Source) -> dict:
+    """A map whose operands include strided views (transposes, slices, a part of a concat):
+    one thread per element of the frame, each operand indexed through its offset and strides
+    (contiguous operands through their row-major strides), NumPy broadcasting right-aligned.
+    The bound symbols are kernel arguments here: view strides may name them."""
+    params_by_name = {p.name: p for p in fn.params}
+    frame = kernel.shape
+    rank = len(frame)
+    dims = P.spell_dims(frame)
+    dtypes = {s.var: s.dtype for s in kernel.program}
+    scalars = _scalar_params(kernel.program, params_by_name)
+    status = needs_status(kernel.program)
+    symbols = [b.symbol for b in fn.bindings]
+    extra = (["int64_t n"] + [f"int64_t sym_{s}" for s in symbols]
+             + [f"{P.ctype(t)} p_{n}" for n, t in scalars] + ["int32_t* status"])
+    name = kernel.name
+    operands = list(kernel.inputs) + [o.operand for o in kernel.outputs]
+    L = [f"static __global__ void __launch_bounds__({THREADS}) {name}_s("
+         + ", ".join(_kernel_params(kernel, extra)) + ") {"]
+    L.append("  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;"
+             " e += (int64_t)gridDim.x * blockDim.x) {")
+    L.append("    int64_t rest = e; (void)rest;")
+    for d in reversed(range(rank)):
+        if frame[d] == 1:
+            L.append(f"    const int64_t i{d} = 0;")
+        else:
+            L.append(f"    const int64_t i{d} = rest % {dims[d]}; rest /= {dims[d]};")
+    for k, operand in enumerate(operands):
+        shape = tuple(operand.shape)
+        if len(shape) > rank:
+            raise ValueError(f"{shape} does not broadcast to {frame}")
+        offset, strides = operand.view if operand.view is not None else (
+            0, P.contiguous_strides(shape))
+        at = offset
+        for j, dim in enumerate(shape):
+            d = j + rank - len(shape)
+            if dim == 1:
+                continue  # a unit axis: index 0 (or broadcast over the frame)
+            if dim != frame[d]:
+                raise ValueError(f"{shape} does not broadcast to {frame}")
+            at = P.term_add(at, P.term_mul(f"i{d}", strides[j]))
+        L.append(f"    const int64_t at{k} = {P.spell_term(at)};")
+    n_in = len(kernel.inputs)
+    for s in kernel.program:
+        if s.op == "input":
+            i = s.args[0]
+            load = f"in{i}[at{i}]"
+            if kernel.inputs[i].dtype == "bf16":
+                load = f"ppyb200::convert<float, __nv_bfloat16>({load})"
+            L.append(f"    const {P.ctype(_compute_dtype(s.dtype))} {s.var} = {load};")
+            continue
+        expr, pre = stmt_expr(s, lambda v: v, dtypes)
+        L.extend("    " + p for p in pre)
+        L.append(f"    const {P.ctype(_compute_dtype(s.dtype))} {s.var} = {expr};")
+    for j, out in enumerate(kernel.outputs):
+        ct = P.ctype(out.operand.dtype)
+        L.append(f"    out{j}[at{n_in + j}] = ppyb200::convert<{ct}, "
+                 f"{P.ctype(_compute_dtype(dtypes[out.var]))}>({out.var});")
+    L.append("  }")
+    L.append("}")
+    src.kernels.append("\n".join(L))
+    args = ([o.pointer for o in kernel.inputs] + [o.operand.pointer for o in kernel.outputs]
+            + ["n"] + [f"sym_{s}" for s in symbols] + [f"p_{n}" for n, _ in scalars]
+            + ["status"])
+    lines = ["{", f"  const int64_t n = {P.spell_count(frame)};", "  if (n > 0) {",
+             f"    {name}_s<<<(unsigned)ppyb200_blocks(n, {THREADS}), {THREADS}, 0, stream>>>("
+             + ", ".join(args) + ");",
+             "    launches++;", "  }", "}"]
+    return {"launch": lines, "status": status}
+
+
 def _map_kernel(kernel: P.MapKernel, fn: P.TensorFunction, src: _Source) -> dict:
     """A flat or 2-D map: returns launch info for the host wrapper."""
+    if any(o.view is not None for o in kernel.inputs) or any(
+            o.operand.view is not None for o in kernel.outputs):
+        return _strided_map_kernel(kernel, fn, src)
     params_by_name = {p.name: p for p in fn.params}
     frame = kernel.shape
     operand_shapes = [o.shape for o in kernel.inputs] + [o.operand.shape for o in kernel.outputs]
@@ -582,6 +656,11 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
             e = f"r{i}"
         else:
             e = f"s{i}"
+        if masked and c in ("elem", "cols"):
+            # a lane past the row's last chunk reads nothing (its values are never folded or
+            # stored, but the read itself would leave the row: past a staged row group's
+            # shared memory, or past the end of a column vector)
+            e = f"((j * TPR + lane < CHUNKS) ? {e} : {ct_i}{{}})"
         if kernel.inputs[i].dtype == "bf16":
             e = f"ppyb200::convert<float, __nv_bfloat16>({e})"
         return e
@@ -1048,6 +1127,8 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
         G.append("  }")
     for param, shape in fn.guards:
         G.append(f"  if ({param}_len < {P.spell_count(shape)}) return PPY_STATUS_FALLBACK;")
+    for symbol, minimum in fn.dim_guards:
+        G.append(f"  if (sym_{symbol} < (int64_t){minimum}) return PPY_STATUS_FALLBACK;")
     counts = {}
     for p in buffers:
         shapes = p.read_shapes + p.write_shapes

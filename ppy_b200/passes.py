@@ -26,7 +26,8 @@ from ppy_compiler.ir.passes import Pass, PassContext
 
 from .scalar_c import Unsupported
 
-__all__ = ["CommonTensorsToBuffers", "common_tensors_to_buffers"]
+__all__ = ["CommonTensorsToBuffers", "common_tensors_to_buffers", "ReductionsToTrailingAxes",
+           "reductions_to_trailing_axes"]
 
 
 def _cast(value, dtype: str):
@@ -153,6 +154,53 @@ class CommonTensorsToBuffers(Pass):
 
     def run(self, module, ctx: PassContext) -> bool:
         changed = common_tensors_to_buffers(module)
+        if changed:
+            ctx.invalidate()
+        return changed
+
+
+def reductions_to_trailing_axes(module) -> bool:
+    """Rewrite every `tensor.reduce` over axes that are neither all of its input's axes nor a
+    leading or trailing run of them into a transpose that moves them last (the kept axes
+    first, both in order) and a reduce over the trailing axes; with keepdims a reshape gives
+    back the unit-axis shape, which has the same layout. Each output element then folds its
+    elements in the row-major order of the reduced axes, as the reference's row-major loop
+    does (lower_tensor.py:733-754). True if anything changed."""
+    changed = False
+    for function in module.functions.values():
+        if function.is_declaration:
+            continue
+        for op in list(function.operations()):
+            if op.name != "tensor.reduce":
+                continue
+            source = op.operands[0]
+            rank = len(tensor_dialect.describe(source.type).shape)
+            axes = tuple(sorted(int(a) for a in op.attributes["axes"]))
+            if (not axes or axes == tuple(range(rank)) or axes == tuple(range(len(axes)))
+                    or axes == tuple(range(rank - len(axes), rank))):
+                continue
+            kept = [d for d in range(rank) if d not in axes]
+            b = Builder().before(op)
+            moved = tensor_dialect.transpose(b, source, tuple(kept) + axes)
+            result = tensor_dialect.reduce(b, moved, tuple(range(len(kept), rank)),
+                                           str(op.attributes["op"]), keepdims=False)
+            if bool(op.attributes.get("keepdims", False)):
+                result = tensor_dialect.reshape(b, result,
+                                                tensor_dialect.describe(op.results[0].type).shape)
+            op.results[0].replace_all_uses_with(result)
+            op.erase()
+            changed = True
+    return changed
+
+
+class ReductionsToTrailingAxes(Pass):
+    """Backend-stage pass: reductions over middle axes become a transpose and a reduction
+    over trailing axes (see `reductions_to_trailing_axes`)."""
+
+    name = "b200-reductions-to-trailing-axes"
+
+    def run(self, module, ctx: PassContext) -> bool:
+        changed = reductions_to_trailing_axes(module)
         if changed:
             ctx.invalidate()
         return changed

@@ -68,6 +68,50 @@ def spell_dims(shape: tuple) -> list[str]:
     return [f"(int64_t){d}" if isinstance(d, int) else f"sym_{d}" for d in shape]
 
 
+# -- index arithmetic of strided views: ints where known, C++ int64_t expressions otherwise ----
+
+
+def dim_term(dim):
+    """A dimension as an index term: an int, or the bound symbol's local."""
+    return dim if isinstance(dim, int) else f"sym_{dim}"
+
+
+def spell_term(x) -> str:
+    return f"(int64_t){x}" if isinstance(x, int) else x
+
+
+def term_mul(a, b):
+    if isinstance(a, int) and isinstance(b, int):
+        return a * b
+    if a == 0 or b == 0:
+        return 0
+    if a == 1:
+        return b
+    if b == 1:
+        return a
+    return f"({spell_term(a)} * {spell_term(b)})"
+
+
+def term_add(a, b):
+    if isinstance(a, int) and isinstance(b, int):
+        return a + b
+    if a == 0:
+        return b
+    if b == 0:
+        return a
+    return f"({spell_term(a)} + {spell_term(b)})"
+
+
+def contiguous_strides(shape: tuple) -> tuple:
+    """Row-major element strides of `shape` (lower_tensor's `shapes.strides_of`)."""
+    strides = [1] * len(shape)
+    running = 1
+    for axis in reversed(range(len(shape))):
+        strides[axis] = running
+        running = term_mul(running, dim_term(shape[axis]))
+    return tuple(strides)
+
+
 @dataclass
 class Param:
     """One IR function parameter and the ABI atoms it becomes."""
@@ -84,12 +128,19 @@ class Param:
 
 @dataclass
 class Operand:
-    """A tensor in memory: a buffer parameter (`param`) or a temporary (`temp`)."""
+    """A tensor in memory: a buffer parameter (`param`) or a temporary (`temp`).
+
+    With `view` = (offset, strides) the tensor is a strided view of that memory (the
+    reference's `_View`, lower_tensor.py:695-714): element (i0, i1, ...) of `shape` sits at
+    offset + i0 * strides[0] + i1 * strides[1] + ..., offset and strides in elements, each an
+    int or a C++ expression over the bound symbols; without it the tensor is contiguous and
+    row-major."""
 
     source: str  # "param" | "temp"
     name: str
     dtype: str
     shape: tuple
+    view: tuple | None = None
 
     @property
     def pointer(self) -> str:
@@ -224,6 +275,9 @@ class TensorFunction:
     temps: list
     kernels: list
     kind: str = "tensor"
+    #: (symbol, minimum): guard `symbol >= minimum` (a slice that stops inside a symbolic
+    #: dimension).
+    dim_guards: list = field(default_factory=list)
 
 
 @dataclass

@@ -92,7 +92,10 @@ def broadcast_shape(a: tuple, b: tuple) -> tuple:
 MAP_OPS = {"tensor.fused", "tensor.unary", "tensor.convert", "tensor.add", "tensor.sub",
            "tensor.mul", "tensor.div", "tensor.pow", "tensor.min", "tensor.max"}
 VIEW_OPS = {"tensor.load", "tensor.fill", "tensor.broadcast", "tensor.reshape",
-            "tensor.shape_cast"}
+            "tensor.shape_cast", "tensor.transpose", "tensor.slice"}
+#: Views onto memory that already exists, read through offsets and strides
+#: (lower_tensor.py:695-714): a map reads them in place, other kernels from a copy.
+STRIDED_OPS = ("tensor.transpose", "tensor.slice")
 REDUCE_OPS = {"tensor.reduce"}
 MATMUL_OPS = {"tensor.matmul", "linalg.matmul"}
 
@@ -138,6 +141,9 @@ class _TensorTranslator:
         self.temps: list[P.Temp] = []
         self.kernels: list = []
         self.values: dict[int, tuple] = {}  # id(value) -> ("param", Param) | ("temp", Temp)
+        #: transposes/slices copied to a contiguous temporary for a kernel that reads rows
+        self.materialized: set[int] = set()
+        self.dim_guards: list = []
 
     def fresh(self, hint: str) -> str:
         self.counter += 1
@@ -178,14 +184,16 @@ class _TensorTranslator:
         groups = self._partition(body)
         self._materialize(body, groups)
         for group in groups:
-            self.kernels.append(self._kernel(group))
+            kernel = self._kernel(group)
+            self.kernels.extend(kernel if isinstance(kernel, list) else [kernel])
         for param in self.params:
             if param.kind == "buffer":
                 reads, writes = bool(param.read_shapes), bool(param.write_shapes)
                 param.role = "inout" if reads and writes else "in" if reads else (
                     "out" if writes else "")
         return P.TensorFunction(fn.name, self.symbol, self.params, result, result_value,
-                                self.bindings, self.guards, self.temps, self.kernels)
+                                self.bindings, self.guards, self.temps, self.kernels,
+                                dim_guards=self.dim_guards)
 
     def _result(self, ret):
         if not ret.operands:
@@ -258,10 +266,20 @@ class _TensorTranslator:
                         user is op for user, _ in operand.uses
                     ):
                         absorbed.add(id(owner))
+        self._decide_copies(body)
         for op in body:
+            if op.name in STRIDED_OPS and id(op.results[0]) in self.materialized:
+                current = None
+                value = op.results[0]
+                groups.append(_Group("map", _shape(tensor_info(value)), ops=[("copy", value)]))
+                continue
             if op.name in VIEW_OPS or op.name == "core.const" or op.name == "tensor.store":
                 continue
             if id(op) in absorbed:
+                continue
+            if op.name == "tensor.concat":
+                current = None
+                groups.append(_Group("concat", _shape(tensor_info(op.results[0])), ops=[op]))
                 continue
             if op.name in MATMUL_OPS:
                 current = None
@@ -313,7 +331,7 @@ class _TensorTranslator:
                 if current is not None and current.kind == "map" and current.frame == shape:
                     current.ops.append(op)
                     continue
-                if current is not None and current.kind == "row" and (
+                if current is not None and current.kind == "row" and not self._reads_view(op) and (
                     shape == current.frame
                     or self._is_rowwise(shape, current.frame, current.reduced)
                 ):
@@ -324,12 +342,105 @@ class _TensorTranslator:
                 continue
             raise Unsupported(f"{op.name}", "the tensor operations of the b200 backend")
         # A stored value no group computes (a loaded or filled tensor) is copied by a map.
-        computed = {id(r) for g in groups for op in g.ops for r in op.results}
+        computed = {id(r) for g in groups for op in g.ops
+                    for r in ([op[1]] if isinstance(op, tuple) else op.results)}
         for op in body:
             if op.name == "tensor.store" and id(op.operands[0]) not in computed:
                 value = op.operands[0]
                 groups.append(_Group("map", _shape(tensor_info(value)), ops=[("copy", value)]))
         return self._fuse_epilogues(groups)
+
+    # ---------------------------------------------------------------- strided views
+
+    def _decide_copies(self, body) -> None:
+        """Transposes and slices that a row, reduction or matmul kernel reads (those read rows
+        of contiguous memory) are copied to a temporary first; maps read them in place."""
+        for op in body:
+            if op.name not in STRIDED_OPS:
+                continue
+            value = op.results[0]
+            for user, _ in value.uses:
+                name = getattr(user, "name", None)
+                feeds_matmul = name == "tensor.convert" and any(
+                    getattr(u, "name", None) in MATMUL_OPS for u, _ in user.results[0].uses)
+                if (_reduce_of(user) is not None or name in MATMUL_OPS or feeds_matmul
+                        or name == "tensor.reshape"):
+                    self.materialized.add(id(value))
+
+    def _reads_view(self, op) -> bool:
+        """Whether `op` reads a transpose or slice in place (through broadcasts)."""
+        for operand in op.operands:
+            value = operand
+            while True:
+                owner = value.owner
+                name = getattr(owner, "name", None)
+                if name in STRIDED_OPS:
+                    if id(value) not in self.materialized:
+                        return True
+                    break
+                if name in ("tensor.broadcast", "tensor.shape_cast", "tensor.reshape"):
+                    value = owner.operands[0]
+                    continue
+                break
+        return False
+
+    def _strided(self, value, own: bool = False):
+        """(base, offset, strides) when `value` is a transpose or slice (through any chain of
+        views) read in place, else None: element (i0, i1, ...) of `value` is element
+        offset + sum(i_k * strides[k]) of the memory of `base` (lower_tensor.py:695-714).
+        `own` reads `value` itself in place even where it is copied (the copy's own read)."""
+        owner = value.owner
+        name = getattr(owner, "name", None)
+        if name not in STRIDED_OPS or (id(value) in self.materialized and not own):
+            return None
+        source = owner.operands[0]
+        base, offset, strides = self._memory_of(source)
+        if name == "tensor.transpose":
+            perm = tuple(int(p) for p in owner.attributes["perm"])
+            return base, offset, tuple(strides[p] for p in perm)
+        starts = tuple(int(v) for v in owner.attributes["starts"])
+        stops = tuple(int(v) for v in owner.attributes["stops"])
+        steps = tuple(int(v) for v in owner.attributes["steps"])
+        for dim, stop in zip(_shape(tensor_info(source)), stops):
+            # a slice that stops inside a symbolic dimension needs that much of it
+            if isinstance(dim, str) and stop > 0 and (dim, stop) not in self.dim_guards:
+                self.dim_guards.append((dim, stop))
+        for start, stride in zip(starts, strides):
+            offset = P.term_add(offset, P.term_mul(start, stride))
+        return base, offset, tuple(P.term_mul(st, step) for st, step in zip(strides, steps))
+
+    def _memory_of(self, value):
+        """(base, offset, strides) of `value` as memory: a view's, or its own row-major
+        layout (through broadcasts, which give stride 0 on the axes they add or widen)."""
+        found = self._strided(value)
+        if found is not None:
+            return found
+        owner = value.owner
+        name = getattr(owner, "name", None)
+        shape = _shape(tensor_info(value))
+        if name in ("tensor.broadcast", "tensor.shape_cast"):
+            inner = owner.operands[0]
+            base, offset, strides = self._memory_of(inner)
+            inner_shape = _shape(tensor_info(inner))
+            if name == "tensor.shape_cast" or len(inner_shape) > len(shape):
+                if self._strided(inner) is not None:
+                    raise Unsupported("a shape cast of a transposed or sliced tensor",
+                                      "transposes and slices of row-major tensors")
+                return base, offset, P.contiguous_strides(shape)
+            pad = len(shape) - len(inner_shape)
+            out = []
+            for d, dim in enumerate(shape):
+                j = d - pad
+                out.append(0 if j < 0 or (inner_shape[j] == 1 and dim != 1) else strides[j])
+            return base, offset, tuple(out)
+        if name == "tensor.reshape":
+            inner = owner.operands[0]
+            if self._strided(inner) is not None:
+                raise Unsupported("a reshape of a transposed or sliced tensor",
+                                  "reshapes of row-major tensors")
+            base, offset, _ = self._memory_of(inner)
+            return base, offset, P.contiguous_strides(shape)
+        return value, 0, P.contiguous_strides(shape)
 
     def _frame_of(self, op) -> tuple:
         """The iteration shape of a reduction: its input's (broadcast) shape."""
@@ -354,7 +465,7 @@ class _TensorTranslator:
             nxt = groups[index + 1] if index + 1 < len(groups) else None
             if group.kind == "matmul" and nxt is not None and nxt.kind == "map" and (
                 nxt.frame == group.frame
-            ):
+            ) and not any(not isinstance(op, tuple) and self._reads_view(op) for op in nxt.ops):
                 product = group.ops[0].results[0]
                 members = {id(op) for op in nxt.ops if not isinstance(op, tuple)}
                 users = [user for user, _ in product.uses]
@@ -375,6 +486,8 @@ class _TensorTranslator:
         for gi, group in enumerate(groups):
             for op in group.ops:
                 if isinstance(op, tuple):
+                    if getattr(op[1].owner, "name", None) in STRIDED_OPS:
+                        owner_group[id(op[1])] = gi  # a view's copy
                     continue
                 for result in op.results:
                     owner_group[id(result)] = gi
@@ -387,6 +500,8 @@ class _TensorTranslator:
         for gi, group in enumerate(groups):
             for op in group.ops:
                 operands = [op[1]] if isinstance(op, tuple) else op.operands
+                if isinstance(op, tuple) and getattr(op[1].owner, "name", None) in STRIDED_OPS:
+                    operands = [op[1].owner.operands[0]]  # a view's copy reads its source
                 for operand in operands:
                     source = self._through_views(operand)
                     og = owner_group.get(id(source))
@@ -397,11 +512,13 @@ class _TensorTranslator:
         self.owner_group = owner_group
 
     def _through_views(self, value):
-        """The value whose memory a view chain reads (broadcast/reshape/shape_cast)."""
+        """The value whose memory a view chain reads (broadcast/reshape/shape_cast, and
+        transposes and slices read in place)."""
         while True:
             owner = value.owner
             name = getattr(owner, "name", None)
-            if name in ("tensor.broadcast", "tensor.reshape", "tensor.shape_cast"):
+            if name in ("tensor.broadcast", "tensor.reshape", "tensor.shape_cast") or (
+                    name in STRIDED_OPS and id(value) not in self.materialized):
                 value = owner.operands[0]
                 continue
             return value
@@ -418,7 +535,36 @@ class _TensorTranslator:
 
     # ---------------------------------------------------------------- kernels
 
+    def _concat_kernels(self, group: _Group) -> list:
+        """`tensor.concat` (lower_tensor.py:716-730): one copy per part into the result's
+        memory at the part's position along the axis (the stored buffer and/or a temporary)."""
+        op = group.ops[0]
+        result = op.results[0]
+        info = tensor_info(result)
+        shape, dtype = _shape(info), dtype_name(info.dtype)
+        axis = int(op.attributes["axis"])
+        strides = P.contiguous_strides(shape)
+        destinations = [("param", p.name, p.dtype) for p in self.stores.get(id(result), [])]
+        if id(result) in self.crossing:
+            temp = self._temp_for(result)
+            destinations.append(("temp", temp.name, dtype))
+        kernels, position = [], 0
+        for k, part in enumerate(op.operands):
+            pshape = _shape(tensor_info(part))
+            builder = _ProgramBuilder(self, _Group("map", pshape, ops=[("copy", part)]))
+            builder.build()
+            var = builder.var_of[id(part)]
+            view = (P.term_mul(position, strides[axis]), strides)
+            outputs = [P.Output(var, P.Operand(source, name, dt, pshape, view=view))
+                       for source, name, dt in destinations]
+            kernels.append(P.MapKernel(f"{self.symbol}_k{len(self.kernels)}_{k}", pshape,
+                                       builder.inputs, builder.program, outputs))
+            position = P.term_add(position, P.dim_term(pshape[axis]))
+        return kernels
+
     def _kernel(self, group: _Group):
+        if group.kind == "concat":
+            return self._concat_kernels(group)
         builder = _ProgramBuilder(self, group)
         name = f"{self.symbol}_k{len(self.kernels)}"
         if group.kind == "matmul":
@@ -508,11 +654,16 @@ class _ProgramBuilder:
         return self.tensor_leaf(value, _shape(tensor_info(value)))
 
     def tensor_leaf(self, value, shape: tuple) -> str:
-        """A tensor read from memory: a loaded parameter or another kernel's temporary."""
+        """A tensor read from memory: a loaded parameter or another kernel's temporary,
+        possibly through a strided view."""
         owner = value.owner
         name = getattr(owner, "name", None)
         if name == "tensor.fill":
             return self.scalar(owner.operands[0])
+        if name in STRIDED_OPS:
+            copying = any(isinstance(op, tuple) and op[1] is value for op in self.group.ops)
+            if copying or id(value) not in self.owner.materialized:
+                return self.view_leaf(value, shape, copying)
         if name in ("tensor.broadcast", "tensor.shape_cast", "tensor.reshape"):
             inner_shape = shape if name == "tensor.reshape" else _shape(tensor_info(owner.operands[0]))
             if name == "tensor.reshape":
@@ -527,6 +678,31 @@ class _ProgramBuilder:
             temp = self.owner._temp_for(value)
             operand = P.Operand("temp", temp.name, temp.dtype, shape)
         key = (operand.source, operand.name, operand.shape)
+        index = self.input_index.get(key)
+        if index is None:
+            index = len(self.inputs)
+            self.inputs.append(operand)
+            self.input_index[key] = index
+        return self.emit("input", (index,), operand.dtype)
+
+    def view_leaf(self, value, shape: tuple, own: bool) -> str:
+        """A transpose or slice read in place: its base memory with an offset and strides."""
+        view_shape = _shape(tensor_info(value))
+        if tuple(shape) != tuple(view_shape):
+            raise Unsupported("a reshape of a transposed or sliced tensor",
+                              "reshapes of row-major tensors")
+        base, offset, strides = self.owner._strided(value, own=own)
+        bowner = base.owner
+        bname = getattr(bowner, "name", None)
+        if bname == "tensor.fill":
+            return self.scalar(bowner.operands[0])
+        if bname == "tensor.load":
+            param = self.owner.param_by_value[id(bowner.operands[0])]
+            operand = P.Operand("param", param.name, param.dtype, view_shape, (offset, strides))
+        else:
+            temp = self.owner._temp_for(base)
+            operand = P.Operand("temp", temp.name, temp.dtype, view_shape, (offset, strides))
+        key = (operand.source, operand.name, operand.shape, operand.view)
         index = self.input_index.get(key)
         if index is None:
             index = len(self.inputs)
@@ -732,7 +908,12 @@ def _is_tensor_function(function) -> bool:
 
 
 def plan_module(module) -> P.ModulePlan:
-    """Plan every defined function of `module`, or raise `Unsupported`."""
+    """Plan every defined function of `module`, or raise `Unsupported`. The backend pass that
+    moves reduced middle axes last runs here too (it changes nothing the second time), for IR
+    that reaches the translator without the backend's passes (a `.ppyir` read directly)."""
+    from .passes import reductions_to_trailing_axes
+
+    reductions_to_trailing_axes(module)
     functions = []
     notes: list[str] = []
     bodies = set()

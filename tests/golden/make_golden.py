@@ -235,6 +235,84 @@ def build_reductions():
     return m
 
 
+def build_views():
+    """Views and copies (f32): transpose, slice, concat, reductions over middle axes, and
+    views read by a row reduction and by a matmul."""
+    from ppy_compiler.ir import F32, I64, BufferType, Builder, IRModule
+    from ppy_compiler.ir import shape as shapes
+    from ppy_compiler.ir.dialects import core, tensor
+
+    n = shapes.Symbol("N")
+    buf = BufferType(F32)
+    T = tensor.tensor_type
+    m = IRModule("views")
+    m.require("tensor", 1)
+
+    def fn(name, params):
+        f = m.add_function(name, [(p, buf) for p in params], [I64])
+        return f, Builder(f.add_entry_block()), f.entry.arguments
+
+    def const(b, value, shape):
+        return tensor.fill(b, core.const(b, value, F32), T(F32, shape))
+
+    # out[N, 32] = a + 2 * b^T, b [32, N]
+    f, b, (a, bb, out) = fn("transpose_add", ("a", "b", "out"))
+    ta = tensor.load(b, a, T(F32, (n, 32)))
+    tbt = tensor.transpose(b, tensor.load(b, bb, T(F32, (32, n))), (1, 0))
+    tensor.store(b, tensor.elementwise(b, "add", ta, tensor.elementwise(
+        b, "mul", const(b, 2.0, (n, 32)), tbt)), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[N, 4, 8] = x permuted (2, 0, 1), x [4, 8, N]
+    f, b, (x, out) = fn("permute3", ("x", "out"))
+    tx = tensor.load(b, x, T(F32, (4, 8, n)))
+    tensor.store(b, tensor.transpose(b, tx, (2, 0, 1)), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[10, 16] = exp(x[2:12, 3:35:2]) - x[0:10, 0:16], x [N, 40] (N >= 12)
+    f, b, (x, out) = fn("slice_exp", ("x", "out"))
+    tx = tensor.load(b, x, T(F32, (n, 40)))
+    odd = tensor.slice_(b, tx, (2, 3), (12, 35), (1, 2))
+    head = tensor.slice_(b, tx, (0, 0), (10, 16), (1, 1))
+    tensor.store(b, tensor.elementwise(b, "sub", tensor.unary(b, "exp", odd), head), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[N, 24] = concat(2 a, b + 1) along the columns, a [N, 16], b [N, 8]
+    f, b, (a, bb, out) = fn("concat_cols", ("a", "b", "out"))
+    ta = tensor.load(b, a, T(F32, (n, 16)))
+    tb = tensor.load(b, bb, T(F32, (n, 8)))
+    left = tensor.elementwise(b, "mul", ta, const(b, 2.0, (n, 16)))
+    right = tensor.elementwise(b, "add", tb, const(b, 1.0, (n, 8)))
+    tensor.store(b, tensor.concat(b, (left, right), 1), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[16, 16] = concat(a, sqrt(|b|)) along the rows, a [6, 16], b [10, 16]
+    f, b, (a, bb, out) = fn("concat_rows", ("a", "b", "out"))
+    ta = tensor.load(b, a, T(F32, (6, 16)))
+    tb = tensor.load(b, bb, T(F32, (10, 16)))
+    tensor.store(b, tensor.concat(b, (ta, tensor.unary(b, "sqrt", tensor.unary(b, "abs", tb))),
+                                  0), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[N, 16] = sum over the middle axis of x [N, 24, 16]
+    f, b, (x, out) = fn("sum_mid", ("x", "out"))
+    tx = tensor.load(b, x, T(F32, (n, 24, 16)))
+    tensor.store(b, tensor.reduce(b, tx, (1,), "add"), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[N, 1, 5, 1] = max over axes 1 and 3 of x [N, 6, 5, 7] (keepdims)
+    f, b, (x, out) = fn("max_split", ("x", "out"))
+    tx = tensor.load(b, x, T(F32, (n, 6, 5, 7)))
+    tensor.store(b, tensor.reduce(b, tx, (1, 3), "max", keepdims=True), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[N] = row sums of x^T, x [32, N]
+    f, b, (x, out) = fn("rowsum_t", ("x", "out"))
+    tx = tensor.load(b, x, T(F32, (32, n)))
+    tensor.store(b, tensor.reduce(b, tensor.transpose(b, tx, (1, 0)), (1,), "add"), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[N, 24] = a^T @ w, a [32, N], w [32, 24]
+    f, b, (a, w, out) = fn("matmul_t", ("a", "w", "out"))
+    ta = tensor.transpose(b, tensor.load(b, a, T(F32, (32, n))), (1, 0))
+    tw = tensor.load(b, w, T(F32, (32, 24)))
+    tensor.store(b, tensor.matmul(b, ta, tw), out)
+    core.ret(b, core.const(b, 0, I64))
+    return m
+
+
 def build_matmul(k: int = 96, n: int = 80):
     """C = A @ B + bias, f32, A [M, K] with M symbolic."""
     from ppy_compiler.ir import F32, I64, BufferType, Builder, IRModule
@@ -438,6 +516,39 @@ def golden_reductions() -> None:
                         status=np.array([s1, s2, s3, s4], np.int32))
 
 
+def golden_views() -> None:
+    write_ppyir(shared_passes(build_views(), False), "views")
+    engine = jit(shared_passes(build_views(), True))
+    rng = np.random.default_rng(4)
+    f32 = np.float32
+    arrays, status = {}, []
+
+    def run(name, inputs, out_shape):
+        out = np.zeros(out_shape, f32)
+        st, _ = call(engine, name, *[x.ravel() for x in inputs], out.ravel())
+        status.append(st)
+        for i, x in enumerate(inputs):
+            arrays[f"{name}_in{i}"] = x
+        arrays[f"{name}_out"] = out
+
+    run("transpose_add", [rng.standard_normal((37, 32)).astype(f32),
+                          rng.standard_normal((32, 37)).astype(f32)], (37, 32))
+    run("permute3", [rng.standard_normal((4, 8, 29)).astype(f32)], (29, 4, 8))
+    run("slice_exp", [rng.standard_normal((13, 40)).astype(f32)], (10, 16))
+    run("concat_cols", [rng.standard_normal((21, 16)).astype(f32),
+                        rng.standard_normal((21, 8)).astype(f32)], (21, 24))
+    run("concat_rows", [rng.standard_normal((6, 16)).astype(f32),
+                        rng.standard_normal((10, 16)).astype(f32)], (16, 16))
+    run("sum_mid", [rng.standard_normal((9, 24, 16)).astype(f32)], (9, 16))
+    x = rng.standard_normal((4, 6, 5, 7)).astype(f32)
+    x[2, 3, 1, 4] = np.nan
+    run("max_split", [x], (4, 1, 5, 1))
+    run("rowsum_t", [rng.standard_normal((32, 50)).astype(f32)], (50,))
+    run("matmul_t", [rng.standard_normal((32, 40)).astype(f32),
+                     rng.standard_normal((32, 24)).astype(f32)], (40, 24))
+    np.savez_compressed(HERE / "views.npz", status=np.array(status, np.int32), **arrays)
+
+
 def golden_matmul() -> None:
     write_ppyir(shared_passes(build_matmul(), False), "matmul")
     engine = jit(shared_passes(build_matmul(), True))
@@ -622,14 +733,20 @@ def golden_collatz(reference: Path) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", type=Path, required=True)
+    parser.add_argument("--only", help="write one fixture (e.g. views) and no other")
     options = parser.parse_args()
     _setup(options.reference)
+    if options.only:
+        globals()[f"golden_{options.only}"]()
+        print("golden fixture written to", HERE)
+        return
     golden_chain()
     golden_gelu()
     golden_rows()
     golden_reductions()
     golden_matmul()
     golden_layernorm()
+    golden_views()
     golden_collatz(options.reference)
     print("golden fixtures written to", HERE)
 

@@ -113,27 +113,26 @@ def test_doctor_lists_the_backend(project):
 
 def test_unsupported_ir_is_refused_with_the_reason(project):
     root, site = project
-    # a transpose that is not a view: the backend names what it cannot take
+    # rows of a symbolic length: the backend names what it cannot take
     (root / "t.ppyir").write_text(textwrap.dedent('''\
         ppyir 1
         module @t
         dialect core 1
         dialect tensor 1
 
-        func @flip(%a: buffer<f32>, %out: buffer<f32>) -> i64 {
+        func @rowsum(%a: buffer<f32>, %out: buffer<f32>) -> i64 {
         ^entry:
-            %0 = tensor.load %a : tensor.tensor<f32, 4, 8>
-            %1 = tensor.transpose %0 {perm = [1, 0]} : tensor.tensor<f32, 8, 4>
-            %2 = tensor.unary %1 {op = "exp"} : tensor.tensor<f32, 8, 4>
-            tensor.store %2, %out
-            %3 = core.const 0 : i64
-            core.ret %3
+            %0 = tensor.load %a : tensor.tensor<f32, 4, N>
+            %1 = tensor.reduce %0 {axes = [1], keepdims = false, op = "add"} : tensor.tensor<f32, 4>
+            tensor.store %1, %out
+            %2 = core.const 0 : i64
+            core.ret %2
         }
         '''))
     done = _ppy(root, site, "build", "t.ppyir", "--backend", "b200", "-o", "out")
     assert done.returncode != 0
     text = done.stdout + done.stderr
-    assert "E1802" in text and "b200" in text and "transpose" in text
+    assert "E1802" in text and "b200" in text and "reduction" in text and "symbolic" in text
 
 
 def test_committed_prebuilt_modules_are_what_the_backend_generates(ppy_compiler, tmp_path):

@@ -213,6 +213,13 @@ def test_large_reductions_against_the_oracle(rt):
     colmax = np.zeros(64, np.float32)
     assert module.colmax(x.ravel(), colmax).status == 0
     assert np.array_equal(colmax, np.abs(x).max(axis=0))
+    # rows of 48: 12 four-float chunks over 8 lanes, so lanes past a row's last chunk idle;
+    # at this size every staged row group and the last rows of the buffer are used
+    y = rng.standard_normal((200_003, 48)).astype(np.float32)
+    bias = rng.standard_normal(48).astype(np.float32)
+    rowmin = np.zeros(200_003, np.float32)
+    assert module.rowmin(y.ravel(), bias, rowmin).status == 0
+    assert np.array_equal(rowmin, (y - bias).min(axis=1))
 
 
 # ---------------------------------------------------------------- parallel.range (config 2)

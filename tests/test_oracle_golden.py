@@ -80,3 +80,34 @@ def test_reduction_fixtures_follow_the_row_major_fold():
     prod = oracle.fold((1 + d["p"] * np.float32(0.125)).astype(np.float32).ravel(), "mul", 0,
                        np.float32)
     assert np.array_equal(d["prod"], prod.reshape(1))
+
+
+def test_view_fixtures_follow_the_strided_views():
+    """views.npz, from the reference's LLVM JIT: transposes and slices are strided reads of the
+    loaded memory, concat copies, reductions over middle axes fold in row-major order."""
+    d = np.load(GOLDEN / "views.npz")
+    assert list(d["status"]) == [0] * 9
+    f32 = np.float32
+    a, b = d["transpose_add_in0"], d["transpose_add_in1"]
+    assert np.array_equal(d["transpose_add_out"], a + f32(2) * oracle.transpose(b, (1, 0)))
+    assert np.array_equal(d["permute3_out"], oracle.transpose(d["permute3_in0"], (2, 0, 1)))
+    x = d["slice_exp_in0"]
+    grown = np.exp(oracle.slice_(x, (2, 3), (12, 35), (1, 2)))
+    want = grown - oracle.slice_(x, (0, 0), (10, 16), (1, 1))
+    # NumPy's and the reference's f32 exp may differ in the last bit: bound it by the exp term
+    assert np.all(np.abs(d["slice_exp_out"] - want) <= 1e-6 * np.maximum(grown, 1))
+    assert np.array_equal(d["concat_cols_out"], oracle.concat(
+        [d["concat_cols_in0"] * f32(2), d["concat_cols_in1"] + f32(1)], 1))
+    assert np.array_equal(d["concat_rows_out"], oracle.concat(
+        [d["concat_rows_in0"], np.sqrt(np.abs(d["concat_rows_in1"]))], 0))
+    assert np.array_equal(d["sum_mid_out"],
+                          oracle.fold_axes(d["sum_mid_in0"], "add", (1,), False, f32))
+    assert np.array_equal(d["max_split_out"],
+                          oracle.fold_axes(d["max_split_in0"], "max", (1, 3), True, f32),
+                          equal_nan=True)
+    assert np.isnan(d["max_split_out"]).sum() == 1
+    assert np.array_equal(d["rowsum_t_out"], oracle.fold_axes(
+        oracle.transpose(d["rowsum_t_in0"], (1, 0)), "add", (1,), False, f32))
+    at = oracle.transpose(d["matmul_t_in0"], (1, 0))
+    assert np.allclose(d["matmul_t_out"], at.astype(np.float64) @ d["matmul_t_in1"], rtol=1e-5,
+                       atol=1e-5)
