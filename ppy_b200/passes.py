@@ -160,7 +160,7 @@ class CommonTensorsToBuffers(Pass):
 
 
 def reductions_to_trailing_axes(module) -> bool:
-    """Rewrite every `tensor.reduce` over axes that are neither all of its input's axes nor a
+    """Rewrite `linalg.dot` as a product and a reduction, and every `tensor.reduce` over axes that are neither all of its input's axes nor a
     leading or trailing run of them into a transpose that moves them last (the kept axes
     first, both in order) and a reduce over the trailing axes; with keepdims a reshape gives
     back the unit-axis shape, which has the same layout. Each output element then folds its
@@ -171,6 +171,16 @@ def reductions_to_trailing_axes(module) -> bool:
         if function.is_declaration:
             continue
         for op in list(function.operations()):
+            if op.name == "linalg.dot":
+                # sum of a[k] * b[k] from zero (lower_tensor.py:792-802): an elementwise
+                # product and a whole-vector add reduction
+                b = Builder().before(op)
+                product = tensor_dialect.elementwise(b, "mul", op.operands[0], op.operands[1])
+                total = tensor_dialect.reduce(b, product, (0,), "add", keepdims=False)
+                op.results[0].replace_all_uses_with(total)
+                op.erase()
+                changed = True
+                continue
             if op.name != "tensor.reduce":
                 continue
             source = op.operands[0]
@@ -194,8 +204,9 @@ def reductions_to_trailing_axes(module) -> bool:
 
 
 class ReductionsToTrailingAxes(Pass):
-    """Backend-stage pass: reductions over middle axes become a transpose and a reduction
-    over trailing axes (see `reductions_to_trailing_axes`)."""
+    """Backend-stage pass: `linalg.dot` becomes a product and a reduction, reductions over
+    middle axes a transpose and a reduction over trailing axes (see
+    `reductions_to_trailing_axes`)."""
 
     name = "b200-reductions-to-trailing-axes"
 

@@ -236,8 +236,8 @@ def build_reductions():
 
 
 def build_views():
-    """Views and copies (f32): transpose, slice, concat, reductions over middle axes, and
-    views read by a row reduction and by a matmul."""
+    """Views and copies (f32): transpose, slice, concat, reductions over middle axes, views
+    read by a row reduction and by a matmul, and `linalg.dot`."""
     from ppy_compiler.ir import F32, I64, BufferType, Builder, IRModule
     from ppy_compiler.ir import shape as shapes
     from ppy_compiler.ir.dialects import core, tensor
@@ -309,6 +309,15 @@ def build_views():
     ta = tensor.transpose(b, tensor.load(b, a, T(F32, (32, n))), (1, 0))
     tw = tensor.load(b, w, T(F32, (32, 24)))
     tensor.store(b, tensor.matmul(b, ta, tw), out)
+    core.ret(b, core.const(b, 0, I64))
+    # out[] = linalg.dot(a, b), a b [1001] (the reference lowers linalg on static shapes)
+    from ppy_compiler.ir.dialects import linalg
+
+    m.require("linalg", 1)
+    f, b, (a, bb, out) = fn("dot", ("a", "b", "out"))
+    ta = tensor.load(b, a, T(F32, (1001,)))
+    tb = tensor.load(b, bb, T(F32, (1001,)))
+    tensor.store(b, linalg.dot(b, ta, tb), out)
     core.ret(b, core.const(b, 0, I64))
     return m
 
@@ -546,6 +555,8 @@ def golden_views() -> None:
     run("rowsum_t", [rng.standard_normal((32, 50)).astype(f32)], (50,))
     run("matmul_t", [rng.standard_normal((32, 40)).astype(f32),
                      rng.standard_normal((32, 24)).astype(f32)], (40, 24))
+    run("dot", [rng.standard_normal(1001).astype(f32), rng.standard_normal(1001).astype(f32)],
+        (1,))
     np.savez_compressed(HERE / "views.npz", status=np.array(status, np.int32), **arrays)
 
 

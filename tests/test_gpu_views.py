@@ -2,7 +2,7 @@
 transposes and slices read in place by a map (strided reads of the loaded memory, the
 reference's `_View`, lower_tensor.py:695-714), concat as one copy per part (:716-730),
 reductions over middle axes as a transposed copy and a row reduction, and views read by a row
-reduction and by a matmul through a contiguous copy. Against the reference's JIT outputs
+reduction and by a matmul through a contiguous copy, and `linalg.dot`. Against the reference's JIT outputs
 (tests/golden/views.npz): bit-exact for copies, extremum and exact arithmetic; the fp32
 tolerance (`within`) for exp, sums and the matmul."""
 
@@ -52,7 +52,7 @@ def test_exact_views_match_the_reference(views, golden, name, count):
 
 
 @pytest.mark.parametrize("name,count", [("slice_exp", 1), ("sum_mid", 1), ("rowsum_t", 1),
-                                        ("matmul_t", 2)])
+                                        ("matmul_t", 2), ("dot", 2)])
 def test_rounded_views_match_the_reference(views, golden, name, count):
     got, want = _run(views, golden, name, count)
     within(got, want)

@@ -86,7 +86,7 @@ def test_view_fixtures_follow_the_strided_views():
     """views.npz, from the reference's LLVM JIT: transposes and slices are strided reads of the
     loaded memory, concat copies, reductions over middle axes fold in row-major order."""
     d = np.load(GOLDEN / "views.npz")
-    assert list(d["status"]) == [0] * 9
+    assert list(d["status"]) == [0] * 10
     f32 = np.float32
     a, b = d["transpose_add_in0"], d["transpose_add_in1"]
     assert np.array_equal(d["transpose_add_out"], a + f32(2) * oracle.transpose(b, (1, 0)))
@@ -108,6 +108,9 @@ def test_view_fixtures_follow_the_strided_views():
     assert np.isnan(d["max_split_out"]).sum() == 1
     assert np.array_equal(d["rowsum_t_out"], oracle.fold_axes(
         oracle.transpose(d["rowsum_t_in0"], (1, 0)), "add", (1,), False, f32))
+    # linalg.dot: the products folded from zero in index order (lower_tensor.py:792-802)
+    assert np.array_equal(d["dot_out"], oracle.fold(d["dot_in0"] * d["dot_in1"], "add", 0,
+                                                    f32).reshape(1))
     at = oracle.transpose(d["matmul_t_in0"], (1, 0))
     assert np.allclose(d["matmul_t_out"], at.astype(np.float64) @ d["matmul_t_in1"], rtol=1e-5,
                        atol=1e-5)
