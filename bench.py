@@ -56,6 +56,9 @@ def _args():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--tp", type=int, default=0,
                    help="gpt2_tp: ranks per tensor-parallel group (0: the widest that fits)")
+    p.add_argument("--exchange", default="nvlink", choices=["nvlink", "nccl"],
+                   help="gpt2_tp: the row-parallel sum fused into the GEMM over NVLink, or "
+                        "an NCCL all-reduce after it")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU-baseline sample length (seconds of host work)")
     return p.parse_args()
@@ -524,6 +527,7 @@ class Gpt2TP(Gpt2):
     metric = "GPT-2-124M forward tokens/s, tensor parallel: batch 32 x 1024, logits out"
     kernel = "gpt2_tp_forward"
     tp = 0
+    exchange = "nvlink"
 
     def inputs(self):
         import torch
@@ -539,10 +543,16 @@ class Gpt2TP(Gpt2):
     def config(self):
         cfg = super().config()
         tokens = self.ids.numel()
+        if self.exchange == "nvlink":
+            exchange = (f"fused: each row-parallel GEMM's epilogue stores its f32 [{tokens}, "
+                        f"768] partial into every rank of its group of {self.tp} over NVLink, "
+                        "then a flag per rank and an in-order sum; 2 per block")
+        else:
+            exchange = (f"2 NCCL all-reduces (sum, f32 [{tokens}, 768]) per block inside "
+                        f"each group of {self.tp}")
         cfg.update(workload="gpt2_124m_forward_tp",
                    parallelism=f"tp{self.tp}" if self.dp == 1 else f"dp{self.dp}xtp{self.tp}",
-                   exchange=f"2 NCCL all-reduces (sum, f32 [{tokens}, 768]) per block inside "
-                            f"each group of {self.tp}")
+                   exchange=exchange)
         return cfg
 
     def setup_device(self, runtime, torch):
@@ -551,7 +561,8 @@ class Gpt2TP(Gpt2):
         group = None
         if self.dist.world > 1:
             group, _ = gpt2_tp.hybrid_groups(self.tp)
-        self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0, group=group)
+        self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0, group=group,
+                                                exchange=self.exchange)
         self.gpt2 = gpt2
         self.dids = self.ids.cuda()
         self.pids = self.ids.pin_memory()
@@ -705,6 +716,7 @@ def run_b200(args, dist: Dist) -> None:
     runtime.set_stream(stream)
     w = WORKLOADS[args.workload](dist)
     w.tp = args.tp
+    w.exchange = args.exchange
     w.inputs()
     w.setup_device(runtime, torch)
     clocks = Clocks(dist.local)
@@ -834,6 +846,9 @@ def run_b200(args, dist: Dist) -> None:
         if dist.world == 1:
             line["cpu_baseline"] = cpu_baseline(w, args.cpu_seconds)
         print(json.dumps(line), flush=True)
+    close = getattr(getattr(w, "model", None), "close", None)
+    if close is not None:
+        close()  # the tensor-parallel exchange buffers: every rank of the group together
     dist.stop()
 
 

@@ -177,6 +177,43 @@ int32_t ppyb200_attention_causal_vt_bf16(const uint16_t *qkv, const uint16_t *vt
 int32_t ppyb200_attention_causal_bf16(const uint16_t *qkv, uint16_t *out, int64_t batch,
                                       int64_t length, int64_t heads, int64_t head_dim);
 
+/* ---------------------------------------------------------------- tensor parallel over NVLink */
+
+/* Bytes of the handle ppyb200_shared_alloc writes (a cudaIpcMemHandle_t). */
+#define PPYB200_SHARED_HANDLE_BYTES 64
+
+/* Zeroed device memory other processes on this node can map: its handle is written into
+ * handle[PPYB200_SHARED_HANDLE_BYTES]; NULL on failure (message in ppyb200_last_error). */
+void *ppyb200_shared_alloc(int64_t bytes, uint8_t *handle);
+void ppyb200_shared_free(void *pointer);
+/* Another process's ppyb200_shared_alloc memory mapped into the current device (peer access
+ * over NVLink); NULL on failure. */
+void *ppyb200_shared_open(const uint8_t *handle);
+void ppyb200_shared_close(void *pointer);
+
+/* The row-parallel linear of GPT-2's tensor-parallel variant (the out and proj projections of
+ * gpt2.ppy:54,57 with their input columns split over `ranks`), one fused kernel: this rank's
+ * partial product a[M,K] @ w[N,K]^T (bf16 in, f32) on tcgen05 tensor cores, every 16-byte
+ * piece of it stored by the epilogue into slots[s] for s < ranks -- slots[s] is this rank's
+ * slot in rank s's exchange buffer, local or a peer's mapped by ppyb200_shared_open, each
+ * [M, N] f32. K % 64 == 0, N % 4 == 0, ranks <= 8; `slots` is a host array. `*status` (may
+ * be NULL) is raised to 2 if the kernel gives up a bounded wait. */
+int32_t ppyb200_tp_partial_scatter(const uint16_t *a, const uint16_t *w, float *const *slots,
+                                   int32_t ranks, int64_t m, int64_t n, int64_t k,
+                                   int32_t *status);
+
+/* After the stream's earlier work: `epoch` into element `rank` of flags[s] (every rank's
+ * int32 flag array, mapped here) for s < ranks, with system-scope release. */
+int32_t ppyb200_tp_signal(int32_t *const *flags, int32_t ranks, int32_t rank, int32_t epoch);
+
+/* Waits (bounded, about 2 s) until flags[0..ranks) of this rank's flag array reach `epoch`,
+ * then x[M,N] += bias[N] + exchange[0] + exchange[1] + ... (slot s at s*M*N floats), summed
+ * in rank order on every rank. A wait given up raises `*status` (may be NULL) to 2 and leaves
+ * x alone. N % 4 == 0; x, bias (may be NULL) and exchange 16-byte aligned. */
+int32_t ppyb200_tp_accumulate(float *x, const float *bias, const float *exchange,
+                              const int32_t *flags, int32_t ranks, int64_t m, int64_t n,
+                              int32_t epoch, int32_t *status);
+
 /* ---------------------------------------------------------------- without allocation */
 
 /* Floats in the fixed device array ppyb200_colmax_abs_f32_noalloc keeps its partials in. */

@@ -15,7 +15,11 @@ LM head:
     layernorms       replicated on the full residual stream
     LM head          vocab-parallel: this rank's slice of the logits
 
-Two all-reduces of the f32 residual stream [tokens, 768] per block. g divides 12 and the local
+Two all-reduces of the f32 residual stream [tokens, 768] per block: NCCL's after each
+row-parallel GEMM (`exchange="nccl"`), or, with `exchange="nvlink"`, none at all -- the GEMM's
+epilogue stores its partial tiles straight into a slot of every rank's exchange buffer over
+NVLink (csrc/tp_exchange.cu), a flag per rank marks them complete, and each rank adds the bias
+and the slots to its residual stream in rank order (the same sum, bit for bit, on every rank). g divides 12 and the local
 widths (768/g and 3072/g) stay multiples of 64 (the tensor-core K step): g in {1, 2, 4}. More
 ranks than that run as data-parallel groups of tensor-parallel ranks (`hybrid_layout`,
 `hybrid_groups`): 8 GPUs as 2 groups of 4, each group with half the batch.
@@ -23,6 +27,7 @@ ranks than that run as data-parallel groups of tensor-parallel ranks (`hybrid_la
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 from . import runtime
@@ -61,6 +66,26 @@ def shard_ranges(config: Config, rank: int, size: int) -> TPShard:
     v0 = rank * per + min(rank, extra)
     return TPShard(rank, size, (rank * hl, (rank + 1) * hl), (rank * fl, (rank + 1) * fl),
                    (v0, v0 + per + (1 if rank < extra else 0)))
+
+
+def _bind_exchange(lib) -> None:
+    if getattr(lib, "_exchange_bound", False):
+        return
+    p, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    lib.ppyb200_shared_alloc.argtypes = [i64, p]
+    lib.ppyb200_shared_alloc.restype = p
+    lib.ppyb200_shared_open.argtypes = [p]
+    lib.ppyb200_shared_open.restype = p
+    lib.ppyb200_shared_close.argtypes = [p]
+    lib.ppyb200_shared_close.restype = None
+    lib.ppyb200_shared_free.argtypes = [p]
+    lib.ppyb200_shared_free.restype = None
+    lib.ppyb200_tp_partial_scatter.argtypes = [p, p, p, i32, i64, i64, i64, p]
+    lib.ppyb200_tp_signal.argtypes = [p, i32, i32, i32]
+    lib.ppyb200_tp_accumulate.argtypes = [p, p, p, p, i32, i64, i64, i32, p]
+    for name in ("ppyb200_tp_partial_scatter", "ppyb200_tp_signal", "ppyb200_tp_accumulate"):
+        getattr(lib, name).restype = i32
+    lib._exchange_bound = True
 
 
 def hybrid_layout(world: int, config: Config = GPT2_124M, tp: int = 0) -> tuple[int, int]:
@@ -124,12 +149,18 @@ class GPT2TensorParallel:
     """This rank's part of a randomly initialised GPT-2 (the same weights as GPT2(config, seed)
     on every rank, then sliced). Call forward on every rank of `group` with the same ids."""
 
-    def __init__(self, config: Config = GPT2_124M, seed: int = 0, group=None) -> None:
+    def __init__(self, config: Config = GPT2_124M, seed: int = 0, group=None,
+                 exchange: str = "nccl") -> None:
         import torch
         import torch.distributed as dist
 
+        if exchange not in ("nccl", "nvlink"):
+            raise ValueError(f"exchange {exchange!r}: 'nccl' or 'nvlink'")
         self.config = config
         self.group = group
+        self.exchange = exchange
+        self._nvlink: dict | None = None
+        self._epoch = 0
         rank = dist.get_rank(group) if dist.is_initialized() else 0
         size = dist.get_world_size(group) if dist.is_initialized() else 1
         self.shard = shard_ranges(config, rank, size)
@@ -142,6 +173,7 @@ class GPT2TensorParallel:
         self.layernorm = full.layernorm
         self.lib = runtime.library()
         _bind(self.lib)
+        _bind_exchange(self.lib)
         self._buffers: dict = {}
         del full
         torch.cuda.empty_cache()
@@ -171,10 +203,87 @@ class GPT2TensorParallel:
         if status != runtime.STATUS_OK:
             raise runtime.B200Error(f"{what}: {runtime.last_error()}")
 
+    # ---------------------------------------------------------------- the NVLink exchange
+
+    def _exchange_state(self, tokens: int) -> dict:
+        """Exchange buffers for `tokens` rows (two parities x one [tokens, width] f32 slot per
+        rank) and the flag arrays: this rank's, and every other rank's mapped here. Made by
+        all ranks of the group together."""
+        import torch.distributed as dist
+
+        if self._nvlink is not None and self._nvlink["tokens"] == tokens:
+            return self._nvlink
+        self.close()
+        lib, size, rank = self.lib, self.shard.size, self.shard.rank
+        slot = tokens * self.config.width
+        handle = (ctypes.c_uint8 * 64)()
+        flag_handle = (ctypes.c_uint8 * 64)()
+        own = lib.ppyb200_shared_alloc(2 * size * slot * 4, handle)
+        flags = lib.ppyb200_shared_alloc(64, flag_handle)
+        if not own or not flags:
+            raise runtime.B200Error(f"exchange buffers: {runtime.last_error()}")
+        gathered = [None] * size
+        dist.all_gather_object(gathered, (bytes(handle), bytes(flag_handle)), group=self.group)
+        buffers, flag_arrays = [], []
+        for s, (bh, fh) in enumerate(gathered):
+            if s == rank:
+                buffers.append(own)
+                flag_arrays.append(flags)
+                continue
+            mapped = lib.ppyb200_shared_open((ctypes.c_uint8 * 64).from_buffer_copy(bh))
+            mapped_flags = lib.ppyb200_shared_open((ctypes.c_uint8 * 64).from_buffer_copy(fh))
+            if not mapped or not mapped_flags:
+                raise runtime.B200Error(f"rank {s}'s exchange buffers: {runtime.last_error()}")
+            buffers.append(mapped)
+            flag_arrays.append(mapped_flags)
+        self._epoch = 0  # the flags start at 0
+        self._nvlink = {"tokens": tokens, "slot": slot, "own": own, "flags": flags,
+                        "buffers": buffers, "flag_arrays": flag_arrays,
+                        "flag_set": (ctypes.c_void_p * size)(*flag_arrays)}
+        return self._nvlink
+
+    def close(self) -> None:
+        """Unmap the other ranks' exchange buffers and free this rank's (all ranks together:
+        a barrier sits between the two)."""
+        import torch
+        import torch.distributed as dist
+
+        state, self._nvlink = self._nvlink, None
+        if state is None:
+            return
+        torch.cuda.synchronize()
+        for s, (buffer, flags) in enumerate(zip(state["buffers"], state["flag_arrays"])):
+            if s != self.shard.rank:
+                self.lib.ppyb200_shared_close(buffer)
+                self.lib.ppyb200_shared_close(flags)
+        dist.barrier(group=self.group)
+        self.lib.ppyb200_shared_free(state["own"])
+        self.lib.ppyb200_shared_free(state["flags"])
+
+    def _row_parallel_nvlink(self, a, w, bias, x, tokens, k, st, what):
+        state = self._exchange_state(tokens)
+        size, rank, slot = self.shard.size, self.shard.rank, state["slot"]
+        self._epoch += 1
+        epoch, parity = self._epoch, self._epoch & 1
+        # this rank's slot, in parity `parity`, of every rank's buffer
+        slots = (ctypes.c_void_p * size)(
+            *[b + 4 * (parity * size + rank) * slot for b in state["buffers"]])
+        lib = self.lib
+        self._check(lib.ppyb200_tp_partial_scatter(a.data_ptr(), w.data_ptr(), slots, size,
+                                                   tokens, self.config.width, k, st), what)
+        self._check(lib.ppyb200_tp_signal(state["flag_set"], size, rank, epoch), what)
+        self._check(lib.ppyb200_tp_accumulate(x.data_ptr(), bias.data_ptr(),
+                                              state["own"] + 4 * parity * size * slot,
+                                              state["flags"], size, tokens, self.config.width,
+                                              epoch, st), what)
+
     def _row_parallel(self, a, w, bias, x, tokens, k, st, what):
         """x <- x + bias + sum over ranks of a_r @ w_r^T (rank 0 keeps x and the bias)."""
         import torch.distributed as dist
 
+        if self.exchange == "nvlink" and self.shard.size > 1:
+            self._row_parallel_nvlink(a, w, bias, x, tokens, k, st, what)
+            return
         c = self.config.width
         if self.shard.rank == 0:
             status = self.lib.ppyb200_linear_residual(a.data_ptr(), w.data_ptr(), bias.data_ptr(),
