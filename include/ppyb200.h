@@ -128,6 +128,17 @@ int32_t ppyb200_matmul_bf16_kmajor(const uint16_t *a, const uint16_t *bt, const 
 /* bt[n*K + k] = b[k*N + n]: a bf16 [K,N] matrix into [N,K] (tiled through shared memory). */
 int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64_t n);
 
+/* Which tensor-core GEMM kernel every bf16 matmul of this library launches (the matmul entry
+ * points, the GPT-2 linear layers, built modules' matmuls): PPYB200_GEMM_BY_SHAPE (the
+ * default) clusters of two CTAs per 256 x 256 tile (tcgen05.mma.cta_group::2) when K >= 2048
+ * and one CTA per 128 x 256 tile otherwise; PPYB200_GEMM_PAIRS and PPYB200_GEMM_SINGLE one of
+ * them always. Process-wide; returns the previous form, or PPYB200_RAISED for another value. */
+#define PPYB200_GEMM_BY_SHAPE 0
+#define PPYB200_GEMM_PAIRS 1
+#define PPYB200_GEMM_SINGLE 2
+int32_t ppyb200_set_gemm_form(int32_t form);
+int32_t ppyb200_gemm_form(void);
+
 /* ---------------------------------------------------------------- GPT-2 pieces */
 
 /* x[t, c] = wte[ids[t], c] + wpe[t % length, c] (bf16 tables, f32 x [tokens, width]): the

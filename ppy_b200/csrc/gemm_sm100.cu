@@ -13,6 +13,8 @@ namespace {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+int32_t g_gemm_form = PPYB200_GEMM_BY_SHAPE;
+
 int32_t finish(cudaError_t error, const char* what, uint64_t launched) {
   if (error != cudaSuccess) return ppyb200_check((int32_t)error, what);
   ppyb200_count_launches(launched);
@@ -22,6 +24,19 @@ int32_t finish(cudaError_t error, const char* what, uint64_t launched) {
 }  // namespace
 
 extern "C" {
+
+int32_t ppyb200_set_gemm_form(int32_t form) {
+  if (form != PPYB200_GEMM_BY_SHAPE && form != PPYB200_GEMM_PAIRS &&
+      form != PPYB200_GEMM_SINGLE) {
+    ppyb200_set_error("ppyb200_set_gemm_form: 0 (by shape), 1 (CTA pairs) or 2 (one CTA)");
+    return PPYB200_RAISED;
+  }
+  const int32_t before = g_gemm_form;
+  g_gemm_form = form;
+  return before;
+}
+
+int32_t ppyb200_gemm_form(void) { return g_gemm_form; }
 
 int32_t ppyb200_transpose_bf16(const uint16_t* b, uint16_t* bt, int64_t k, int64_t n) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(ppyb200_stream());

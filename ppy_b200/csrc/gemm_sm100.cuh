@@ -31,6 +31,7 @@
 #include <type_traits>
 
 #include "ppyb200_device.cuh"
+#include "../../include/ppyb200.h"
 
 namespace ppyb200 {
 namespace gemm {
@@ -103,7 +104,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase of `parity` to complete, at most WAIT_LIMIT tries; on giving up (or
 // when another role already gave up) raise the abort flag and the status word.
-__device__ __forceinline__ bool mbar_wait(Shared& s, uint64_t* bar, uint32_t parity,
+template <class Layout>
+__device__ __forceinline__ bool mbar_wait(Layout& s, uint64_t* bar, uint32_t parity,
                                           int32_t* status) {
   for (uint32_t tries = 0; tries < WAIT_LIMIT; ++tries) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -239,6 +241,66 @@ struct BiasEpilogue {
 };
 
 
+// One accumulator tile's epilogue for one warp: the 32 rows of its lane quarter (from row0,
+// `rows` of them inside C), the half of the BN columns from col0 + half * BN / 2; `acc` is the
+// TMEM address of the quarter's lanes at the accumulator's first column.
+template <class Epi>
+__device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows)[EPI_PITCH],
+                                              uint32_t acc, int half, int lane, int64_t row0,
+                                              int64_t col0, int64_t rows, int64_t n) {
+#pragma unroll 1
+  for (int c4 = 0; c4 < BN / 64; ++c4) {
+    const int chunk = half * (BN / 64) + c4;
+    uint32_t r[32];
+    tmem_ld32(acc + (uint32_t)(chunk * 32), r);
+    if constexpr (takes_rows<Epi>::value) {
+      // lane holds row (row0 + lane), columns chunk*32 .. +31, as the epilogue takes them
+      const int64_t col = col0 + chunk * 32;
+      if (lane < rows && col < n) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        epi.store_row(v, row0 + lane, col, n - col < 32 ? n - col : 32);
+      }
+    } else if constexpr (takes_quads<Epi>::value) {
+      // 32 rows x 8 float4 in shared memory, the float4 slot XOR-swizzled by the row so that
+      // both the row-wise writes and the column-wise reads are free of bank conflicts
+      float4* quad = reinterpret_cast<float4*>(&stage_rows[0][0]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        quad[lane * 8 + (q ^ (lane & 7))] =
+            make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+      __syncwarp();
+      const int64_t col = col0 + chunk * 32 + 4 * (lane & 7);
+      float4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = (lane >> 3) + 4 * i;
+        v[i] = quad[rr * 8 + ((lane & 7) ^ (rr & 7))];
+      }
+      __syncwarp();
+      // rows (lane >> 3) + 4 i inside C: i < (rows - (lane >> 3) + 3) / 4
+      const int count = rows > (lane >> 3) ? (int)((rows - (lane >> 3) + 3) / 4) : 0;
+      if (col < n && count > 0) epi.store_quads(v, row0 + (lane >> 3), count < 8 ? count : 8, col);
+    } else {
+      // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
+      // memory so that lane j then holds column chunk*32 + j of all 32 rows
+#pragma unroll
+      for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
+      __syncwarp();
+      const int64_t col = col0 + chunk * 32 + lane;
+      if (col < n && rows > 0) {
+        float column[32];
+#pragma unroll
+        for (int rr = 0; rr < 32; ++rr) column[rr] = stage_rows[rr][lane];
+        epi.store_column(column, row0, col, rows);
+      }
+      __syncwarp();
+    }
+  }
+}
+
 template <class Epi>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -355,58 +417,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t row0 = mb * BM + quarter * 32;
       const int64_t col0 = nb * BN;
       const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-#pragma unroll 1
-      for (int c4 = 0; c4 < BN / 64; ++c4) {
-        const int chunk = half * (BN / 64) + c4;
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS + chunk * 32),
-                  r);
-        if constexpr (takes_rows<Epi>::value) {
-          // lane holds row (row0 + lane), columns chunk*32 .. +31, as the epilogue takes them
-          const int64_t col = col0 + chunk * 32;
-          if (lane < rows && col < n) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            epi.store_row(v, row0 + lane, col, n - col < 32 ? n - col : 32);
-          }
-        } else if constexpr (takes_quads<Epi>::value) {
-          // 32 rows x 8 float4 in shared memory, the float4 slot XOR-swizzled by the row so that
-          // both the row-wise writes and the column-wise reads are free of bank conflicts
-          float4* quad = reinterpret_cast<float4*>(&stage_rows[0][0]);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            quad[lane * 8 + (q ^ (lane & 7))] =
-                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                            __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-          __syncwarp();
-          const int64_t col = col0 + chunk * 32 + 4 * (lane & 7);
-          float4 v[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int rr = (lane >> 3) + 4 * i;
-            v[i] = quad[rr * 8 + ((lane & 7) ^ (rr & 7))];
-          }
-          __syncwarp();
-          // rows (lane >> 3) + 4 i inside C: i < (rows - (lane >> 3) + 3) / 4
-          const int count = rows > (lane >> 3) ? (int)((rows - (lane >> 3) + 3) / 4) : 0;
-          if (col < n && count > 0) epi.store_quads(v, row0 + (lane >> 3), count < 8 ? count : 8, col);
-        } else {
-          // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
-          // memory so that lane j then holds column chunk*32 + j of all 32 rows
-#pragma unroll
-          for (int j = 0; j < 32; ++j) stage_rows[lane][j] = __uint_as_float(r[j]);
-          __syncwarp();
-          const int64_t col = col0 + chunk * 32 + lane;
-          if (col < n && rows > 0) {
-            float column[32];
-#pragma unroll
-            for (int rr = 0; rr < 32; ++rr) column[rr] = stage_rows[rr][lane];
-            epi.store_column(column, row0, col, rows);
-          }
-          __syncwarp();
-        }
-      }
+      epilogue_tile(epi, stage_rows,
+                    tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
+                    lane, row0, col0, rows, n);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.acc_empty[a]);
@@ -417,6 +430,229 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ---- the 2-CTA form: a cluster of two CTAs on two SMs computes 256 x 256 tiles with
+// tcgen05.mma.cta_group::2 (M = 256: each CTA holds 128 rows of A and 128 rows of B^T in its
+// shared memory and 128 rows of the accumulator in its TMEM). Per CTA a K-step moves 32 KB
+// instead of 48 KB for the same 128 x 256 x 64 of work: the operand bytes that bound the
+// one-CTA kernel at small K shrink by a third.
+//   both CTAs' warp 0   TMA loads of their halves, completing on the first CTA's `full`
+//                       barrier (the cta_group::2 form of the load; no multicast)
+//   first CTA's warp 1  the MMAs; each commit arrives on the barrier in both CTAs
+//   both CTAs' warps 2-9  the epilogue of their own 128 rows; they release the accumulator
+//                       on the first CTA's `acc_empty`
+// Every wait is bounded as in the one-CTA kernel; the two CTAs meet at cluster barriers only
+// before and after their loops, which every path leaves.
+constexpr int PAIR_STAGES = 5;
+constexpr int PAIR_B_BYTES = (BN / 2) * BK * 2;
+constexpr int PAIR_STAGE_BYTES = A_BYTES + PAIR_B_BYTES;
+constexpr uint32_t PAIR_IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
+                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+
+struct PairShared {
+  alignas(1024) uint8_t stage[PAIR_STAGES][PAIR_STAGE_BYTES];
+  float epi[EPI_WARPS][32][EPI_PITCH];
+  alignas(8) uint64_t full[PAIR_STAGES];
+  alignas(8) uint64_t empty[PAIR_STAGES];
+  alignas(8) uint64_t acc_full[2];
+  alignas(8) uint64_t acc_empty[2];
+  alignas(8) uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of the variable at `addr` in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(PAIR_IDESC), "r"(accumulate));
+}
+
+// Arrive on `bar` (same offset) in both CTAs of the pair once this thread's MMAs are done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                            const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
+                            int64_t k, Epi epi, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  PairShared& s = *reinterpret_cast<PairShared*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool first = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int64_t m_blocks = (m + 2 * BM - 1) / (2 * BM), n_blocks = (n + BN - 1) / BN;
+  const int64_t k_blocks = k / BK, tiles = m_blocks * n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PAIR_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 2 * EPI_WARPS);  // both CTAs' epilogue warps
+    }
+    mbar_init(&s.drain, 1);
+    s.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    // both CTAs, the same warp: one allocation spanning the pair
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the barriers of both CTAs exist before any load or commit reaches them
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- loader (both CTAs): this CTA's 128 rows of A and of B^T
+      uint64_t it = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < tiles && ok; t += pairs) {
+        int64_t mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int st = (int)(it % PAIR_STAGES);
+          const uint32_t phase = (uint32_t)((it / PAIR_STAGES) & 1);
+          if (!mbar_wait(s, &s.empty[st], phase ^ 1, status)) {
+            ok = false;
+            break;
+          }
+          if (first) mbar_expect_tx(&s.full[st], 2 * PAIR_STAGE_BYTES);
+          const uint32_t bar = mapa_shared(smem_u32(&s.full[st]), 0);
+          tma_load_2d_pair(s.stage[st], &map_a, bar, (int32_t)(kb * BK),
+                           (int32_t)(mb * 2 * BM + rank * BM));
+          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, (int32_t)(kb * BK),
+                           (int32_t)(nb * BN + rank * (BN / 2)));
+        }
+      }
+      // the pair's copies land before the CTAs may leave (they all complete on the first
+      // CTA's barriers; the second CTA leaves only after the cluster barrier below)
+      if (first) {
+        const uint64_t from = it > (uint64_t)PAIR_STAGES ? it - PAIR_STAGES : 0;
+        for (uint64_t j = from; j < it; ++j)
+          mbar_drain_wait(&s.full[j % PAIR_STAGES], (uint32_t)((j / PAIR_STAGES) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      if (first) {
+        // ---- MMA issuer (first CTA)
+        uint64_t it = 0, acc_it = 0;
+        bool ok = true;
+        for (int64_t t = pair; t < tiles && ok; t += pairs, ++acc_it) {
+          const int a = (int)(acc_it & 1);
+          const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+          if (!mbar_wait(s, &s.acc_empty[a], aphase ^ 1, status)) break;
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(a * ACC_COLS);
+          for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+            const int st = (int)(it % PAIR_STAGES);
+            const uint32_t phase = (uint32_t)((it / PAIR_STAGES) & 1);
+            if (!mbar_wait(s, &s.full[st], phase, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t adesc = smem_desc(s.stage[st]);
+            const uint64_t bdesc = smem_desc(s.stage[st] + A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk)
+              mma_bf16_pair(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
+                            (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_commit_pair(&s.empty[st]);
+          }
+          if (ok) mma_commit_pair(&s.acc_full[a]);
+        }
+        mma_commit_pair(&s.drain);
+      }
+      // every MMA writing this CTA's TMEM has finished before it is freed
+      mbar_drain_wait(&s.drain, 0);
+    }
+  } else {
+    // ---- epilogue (both CTAs): this CTA's 128 rows of each 256 x 256 tile
+    const int quarter = warp & 3;
+    const int ew = warp - 2;
+    const int half = ew >> 2;
+    float(*stage_rows)[EPI_PITCH] = s.epi[ew];
+    uint64_t acc_it = 0;
+    for (int64_t t = pair; t < tiles; t += pairs, ++acc_it) {
+      const int a = (int)(acc_it & 1);
+      const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+      if (!mbar_wait(s, &s.acc_full[a], aphase, status)) break;
+      tc_fence_after();
+      int64_t mb, nb;
+      tile_coords(t, m_blocks, n_blocks, mb, nb);
+      const int64_t row0 = mb * 2 * BM + rank * BM + quarter * 32;
+      const int64_t col0 = nb * BN;
+      const int64_t rows = m - row0 < 32 ? m - row0 : 32;
+      epilogue_tile(epi, stage_rows,
+                    tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
+                    lane, row0, col0, rows, n);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[a]), 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs are done with the pair's TMEM and barriers
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TMEM_COLS));
   }
 }
@@ -464,12 +700,12 @@ inline bool tileable(int64_t m, int64_t n, int64_t k) {
 
 inline size_t shared_bytes() { return sizeof(Shared) + 1024; }
 
-// Launch on `stream`; returns a cudaError_t (cudaErrorInvalidValue when the maps cannot be
-// made). The caller checks `tileable` and 16-byte alignment of a, bt first.
+// The one-CTA kernel on `stream`; returns a cudaError_t (cudaErrorInvalidValue when the maps
+// cannot be made). The caller checks `tileable` and 16-byte alignment of a, bt first.
 template <class Epi>
-inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m, int64_t n,
-                          int64_t k, Epi epi, int32_t* status, int sm_count,
-                          cudaStream_t stream) {
+inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m,
+                                 int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
+                                 cudaStream_t stream) {
   CUtensorMap map_a, map_b;
   if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN))
     return cudaErrorInvalidValue;
@@ -486,6 +722,64 @@ inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64
   matmul_bf16_kernel<Epi><<<grid, THREADS, shared_bytes(), stream>>>(map_a, map_b, m, n, k, epi,
                                                                      status);
   return cudaGetLastError();
+}
+
+inline size_t pair_shared_bytes() { return sizeof(PairShared) + 1024; }
+
+// K from which CTA pairs run by default: with K = 3072 and 8192 they measured 3 % and 2.4 %
+// faster than one CTA per tile; at K = 768 (short loops whose epilogues set the pace) equal
+// or slower.
+constexpr int64_t PAIR_MIN_K = 2048;
+
+
+// The 2-CTA kernel on `stream`: clusters of two CTAs, as many as can be resident at once (at
+// most one per 256 x 256 tile). Same contract as `launch`.
+template <class Epi>
+inline cudaError_t launch_pair(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m,
+                               int64_t n, int64_t k, Epi epi, int32_t* status,
+                               cudaStream_t stream) {
+  CUtensorMap map_a, map_b;
+  if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN / 2))
+    return cudaErrorInvalidValue;
+  static int max_clusters = 0;
+  cudaLaunchConfig_t config = {};
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = 2;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  config.blockDim = dim3(THREADS, 1, 1);
+  config.dynamicSmemBytes = pair_shared_bytes();
+  config.stream = stream;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  if (max_clusters == 0) {
+    cudaError_t e = cudaFuncSetAttribute(matmul_bf16_pair_kernel<Epi>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)pair_shared_bytes());
+    if (e != cudaSuccess) return e;
+    config.gridDim = dim3(2, 1, 1);
+    e = cudaOccupancyMaxActiveClusters(&max_clusters, matmul_bf16_pair_kernel<Epi>, &config);
+    if (e != cudaSuccess) return e;
+    if (max_clusters < 1) return cudaErrorInvalidConfiguration;
+  }
+  const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
+  const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
+  config.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  return cudaLaunchKernelEx(&config, matmul_bf16_pair_kernel<Epi>, map_a, map_b, m, n, k, epi,
+                            status);
+}
+
+// The tensor-core GEMM: CTA pairs or one CTA per tile, as ppyb200_gemm_form() says (by K by
+// default). Same contract as `launch_single`.
+template <class Epi>
+inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m, int64_t n,
+                          int64_t k, Epi epi, int32_t* status, int sm_count,
+                          cudaStream_t stream) {
+  const int32_t form = ppyb200_gemm_form();
+  if (form == PPYB200_GEMM_PAIRS || (form == PPYB200_GEMM_BY_SHAPE && k >= PAIR_MIN_K))
+    return launch_pair(a, bt, m, n, k, epi, status, stream);
+  return launch_single(a, bt, m, n, k, epi, status, sm_count, stream);
 }
 
 }  // namespace gemm

@@ -29,6 +29,8 @@ def lib():
         getattr(lib, name).restype = ctypes.c_int32
     lib.ppyb200_transpose_bf16.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                            ctypes.c_int64]
+    lib.ppyb200_set_gemm_form.argtypes = [ctypes.c_int32]
+    lib.ppyb200_set_gemm_form.restype = ctypes.c_int32
     return lib
 
 
@@ -101,6 +103,35 @@ def test_tensor_cores_take_ragged_m_and_n(lib, m, n, k):
     torch.cuda.synchronize()
     _check(out[:m], _reference(a, b, bias), rel=1e-4)
     assert torch.all(out[m] == 7.0)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (512, 768, 768), (300, 520, 192),
+                                   (1, 50257, 128), (130, 131, 128), (1000, 2304, 3072)])
+def test_cta_pairs_match_single_ctas(lib, m, n, k):
+    """The 2-CTA kernel (256 x 256 tiles, tcgen05.mma.cta_group::2) against the one-CTA kernel
+    and float64: aligned, ragged and deep-K shapes, bias added, one row past C untouched."""
+    a, b, bias = _operands(m, n, k, seed=9)
+    da, dbt, dbias = a.cuda(), b.t().contiguous().cuda(), bias.cuda()
+    outs = []
+    try:
+        for form in (2, 1):  # one CTA per tile, then CTA pairs
+            assert lib.ppyb200_set_gemm_form(form) in (0, 1, 2)
+            out = torch.full((m + 1, n), 7.0, device="cuda")
+            assert lib.ppyb200_matmul_bf16_kmajor(_ptr(da), _ptr(dbt), _ptr(dbias), _ptr(out),
+                                                  m, n, k) == 0
+            torch.cuda.synchronize()
+            outs.append(out)
+    finally:
+        lib.ppyb200_set_gemm_form(0)
+    one, pair = outs
+    assert torch.all(pair[m] == 7.0)
+    _check(pair[:m], _reference(a, b, bias), rel=1e-4)
+    assert torch.allclose(pair, one, rtol=1e-5, atol=1e-5)
+
+
+def test_gemm_form_refuses_other_values(lib):
+    assert lib.ppyb200_set_gemm_form(3) == -1
+    assert lib.ppyb200_set_gemm_form(0) == 0  # by shape, the default
 
 
 @pytest.mark.parametrize("offset", [4, 36, 1])
