@@ -377,7 +377,7 @@ class Gemm(Workload):
     metric = "matmul TFLOP/s: C = A @ B + bias, bf16 A/B, f32 accumulate and C, 8192^3"
     unit = "TFLOP/s"
     dtype = "bf16"
-    kernel = "matmul_bf16_kernel"
+    kernel = "matmul_bf16_pair_kernel"  # K = 8192: CTA pairs
     M = N = K = 8192
     flops = 2 * 8192 ** 3
 
