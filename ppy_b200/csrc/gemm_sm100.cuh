@@ -29,6 +29,7 @@
 #include <stdint.h>
 
 #include <type_traits>
+#include <utility>
 
 #include "ppyb200_device.cuh"
 #include "../../include/ppyb200.h"
@@ -218,6 +219,26 @@ template <class E, class = void>
 struct takes_quads : std::false_type {};
 template <class E>
 struct takes_quads<E, std::void_t<decltype(E::kQuads)>> : std::integral_constant<bool, E::kQuads> {};
+// Or, for bf16 C whose rows start on 16-byte boundaries and N % 64 == 0, it may hand over whole
+// 128-byte lines: with `static constexpr bool kLines = true`, members `__nv_bfloat16* out` and
+// `int64_t ldo`, and `pack32(const float (&acc)[32], int64_t col0, uint32_t (&pk)[16])` giving
+// the bf16 pairs of 32 columns of one row (bias and activation applied), the kernel takes two
+// adjacent 32-column chunks at a time -- 64 bf16, one line of each row --, turns the 32 rows'
+// lines through shared memory (16-byte slots XOR-swizzled by the row) and stores them eight
+// lanes per line: each 16-byte store instruction of the warp writes four whole lines, where
+// the row form writes 16 bytes into each of 32 rows and leaves every sector it touches half
+// written until its next instruction.
+template <class E, class = void>
+struct takes_lines : std::false_type {};
+template <class E>
+struct takes_lines<E, std::void_t<decltype(E::kLines)>> : std::integral_constant<bool, E::kLines> {};
+// A kLines epilogue may also have `bool is_line(int64_t col)`: where it is false, the pair of
+// chunks from `col` goes to its `store_row` (the row form) instead.
+template <class E, class = void>
+struct has_is_line : std::false_type {};
+template <class E>
+struct has_is_line<E, std::void_t<decltype(std::declval<const E&>().is_line(int64_t{}))>>
+    : std::true_type {};
 
 template <class Epi>
 __device__ __forceinline__ void for_column(const Epi& epi, const float (&acc)[32], int64_t row0,
@@ -248,6 +269,71 @@ template <class Epi>
 __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows)[EPI_PITCH],
                                               uint32_t acc, int half, int lane, int64_t row0,
                                               int64_t col0, int64_t rows, int64_t n) {
+  if constexpr (takes_lines<Epi>::value) {
+    uint4* line = reinterpret_cast<uint4*>(&stage_rows[0][0]);  // 32 rows x 8 slots of 16 B
+    const int slot = lane & 7;
+#pragma unroll 1
+    for (int c2 = 0; c2 < BN / 64; c2 += 2) {
+      const int chunk = half * (BN / 64) + c2;
+      const int64_t col = col0 + chunk * 32;  // the line's first column (N % 64 == 0: whole)
+      if constexpr (has_is_line<Epi>::value) {
+        if (!epi.is_line(col)) {  // the same for the whole warp: it depends on col alone
+#pragma unroll 1
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t r[32];
+            tmem_ld32(acc + (uint32_t)((chunk + h2) * 32), r);
+            const int64_t c = col + 32 * h2;
+            if (lane < rows && c < n) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              epi.store_row(v, row0 + lane, c, n - c < 32 ? n - c : 32);
+            }
+          }
+          continue;
+        }
+      }
+      uint32_t pk0[16], pk1[16];
+      {
+        uint32_t r[32];
+        float v[32];
+        tmem_ld32(acc + (uint32_t)(chunk * 32), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (col < n) epi.pack32(v, col, pk0);
+        tmem_ld32(acc + (uint32_t)(chunk * 32 + 32), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (col < n) epi.pack32(v, col + 32, pk1);
+      }
+      if (col < n) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          line[lane * 8 + (q ^ (lane & 7))] =
+              make_uint4(pk0[4 * q], pk0[4 * q + 1], pk0[4 * q + 2], pk0[4 * q + 3]);
+          line[lane * 8 + ((q + 4) ^ (lane & 7))] =
+              make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
+        }
+      }
+      __syncwarp();
+      if (col < n) {
+        uint4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = (lane >> 3) + 4 * i;
+          v[i] = line[rr * 8 + (slot ^ (rr & 7))];
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = (lane >> 3) + 4 * i;
+          if (rr < rows)
+            *reinterpret_cast<uint4*>(epi.out + (row0 + rr) * epi.ldo + col + 8 * slot) = v[i];
+        }
+      }
+      __syncwarp();
+    }
+    return;
+  }
 #pragma unroll 1
   for (int c4 = 0; c4 < BN / 64; ++c4) {
     const int chunk = half * (BN / 64) + c4;
@@ -283,7 +369,7 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows
       // rows (lane >> 3) + 4 i inside C: i < (rows - (lane >> 3) + 3) / 4
       const int count = rows > (lane >> 3) ? (int)((rows - (lane >> 3) + 3) / 4) : 0;
       if (col < n && count > 0) epi.store_quads(v, row0 + (lane >> 3), count < 8 ? count : 8, col);
-    } else {
+    } else if constexpr (!takes_lines<Epi>::value) {
       // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
       // memory so that lane j then holds column chunk*32 + j of all 32 rows
 #pragma unroll

@@ -180,6 +180,30 @@ struct LinearBf16Rows {  // ldo % 8 == 0, out and bias 16-byte aligned
   }
 };
 
+// The same bf16 outputs handed to the kernel as whole 128-byte lines (the kLines form):
+// N % 64 == 0, ldo % 8 == 0, out and bias 16-byte aligned.
+template <int ACTIVATION>
+struct LinearBf16Lines {
+  static constexpr bool kLines = true;
+  const float* bias;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  __device__ __forceinline__ void pack32(const float (&acc)[32], int64_t col0,
+                                         uint32_t (&pk)[16]) const {
+    float b[32];
+    load_bias32(bias, col0, b);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float v0 = acc[2 * k] + b[2 * k], v1 = acc[2 * k + 1] + b[2 * k + 1];
+      if (ACTIVATION == 1) {
+        v0 = gelu_tanh(v0);
+        v1 = gelu_tanh(v1);
+      }
+      pk[k] = pack_bf16x2(v0, v1);
+    }
+  }
+};
+
 struct LinearResidualQuads {  // ld % 4 == 0, N % 4 == 0, residual and bias 16-byte aligned
   static constexpr bool kQuads = true;
   const float* bias;
@@ -213,28 +237,29 @@ struct LinearResidualQuads {  // ld % 4 == 0, N % 4 == 0, residual and bias 16-b
 // of the attention kernel's P.V product. The 32 rows a warp holds are consecutive tokens of one
 // sequence (length % 32 == 0), so each store of a v column covers 64 contiguous bytes of vt.
 struct LinearQkv {
-  static constexpr bool kRows = true;
+  static constexpr bool kLines = true;
   const float* bias;
-  __nv_bfloat16* qkv;
+  __nv_bfloat16* out;  // qkv [tokens, 3 * width]: its q and k columns, as whole lines
   __nv_bfloat16* vt;
+  int64_t ldo;  // 3 * width
   int64_t width, length, heads;
-  // a lane holds 32 consecutive columns of one token's row; the chunk lies inside q, k or one
-  // head of v (width and the head size are multiples of 32)
+  // q and k leave as whole 128-byte lines of qkv; the v columns in the row form below
+  __device__ __forceinline__ bool is_line(int64_t col) const { return col < 2 * width; }
+  __device__ __forceinline__ void pack32(const float (&acc)[32], int64_t col0,
+                                         uint32_t (&pk)[16]) const {
+    float b[32];
+    load_bias32(bias, col0, b);
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      pk[k] = pack_bf16x2(acc[2 * k] + b[2 * k], acc[2 * k + 1] + b[2 * k + 1]);
+  }
+  // v: column d of head h goes to vt row (b * heads + h) * 64 + d at position l; the lanes of
+  // a warp hold consecutive tokens, so each store covers 64 contiguous bytes (a lane holds 32
+  // consecutive columns of one token's row, inside one head: the head size is 64)
   __device__ __forceinline__ void store_row(const float (&acc)[32], int64_t row, int64_t col0,
                                             int64_t cols) const {
     float b[32];
     load_bias32(bias, col0, b);
-    if (col0 < 2 * width) {
-      uint32_t pk[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) pk[k] = pack_bf16x2(acc[2 * k] + b[2 * k], acc[2 * k + 1] + b[2 * k + 1]);
-      uint4* dst = reinterpret_cast<uint4*>(qkv + row * 3 * width + col0);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-      return;
-    }
-    // v: column d of head h goes to vt row (b * heads + h) * 64 + d at position l; the lanes of
-    // a warp hold consecutive tokens, so each store covers 64 contiguous bytes
     const int64_t hd = col0 - 2 * width;
     const int64_t bi = row / length, l = row - bi * length;
     __nv_bfloat16* dst = vt + ((bi * heads + (hd >> 6)) * 64 + (hd & 63)) * length + l;
@@ -302,8 +327,15 @@ int32_t ppyb200_linear_bf16(const uint16_t* a, const uint16_t* w, const float* b
   }
   auto* O = reinterpret_cast<__nv_bfloat16*>(out);
   const bool rows = n % 8 == 0 && aligned16(out) && (bias == nullptr || aligned16(bias));
+  const bool lines = rows && n % 64 == 0;
   cudaError_t e;
-  if (activation == 1 && rows)
+  if (activation == 1 && lines)
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16Lines<1>{bias, O, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  else if (lines)
+    e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16Lines<0>{bias, O, n}, status,
+                              ppyb200_sm_count(), stream_now());
+  else if (activation == 1 && rows)
     e = ppyb200::gemm::launch(A, W, m, n, k, LinearBf16Rows<1>{bias, O, n}, status,
                               ppyb200_sm_count(), stream_now());
   else if (rows)
@@ -351,7 +383,7 @@ int32_t ppyb200_linear_qkv_bf16(const uint16_t* a, const uint16_t* w, const floa
     return PPYB200_RAISED;
   }
   LinearQkv epi{bias, reinterpret_cast<__nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(vt),
-                width, length, heads};
+                3 * width, width, length, heads};
   return finish(ppyb200::gemm::launch(reinterpret_cast<const __nv_bfloat16*>(a),
                                       reinterpret_cast<const __nv_bfloat16*>(w), m, n, k, epi,
                                       status, ppyb200_sm_count(), stream_now()),

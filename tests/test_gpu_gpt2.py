@@ -147,9 +147,12 @@ def test_embed(lib):
     assert int(status.item()) == 2
 
 
+@pytest.mark.parametrize("m,n", [(512, 3072), (300, 704), (257, 1000)])
 @pytest.mark.parametrize("activation", [0, 1])
-def test_linear_bf16(lib, activation):
-    m, n, k = 512, 3072, 768
+def test_linear_bf16(lib, activation, m, n):
+    """N % 64 == 0 takes whole 128-byte lines (3072; 704 ends inside the last 256-wide tile),
+    other N % 8 == 0 the row form (1000); M ragged."""
+    k = 768
     g = torch.Generator(device="cuda").manual_seed(2)
     a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
     w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(torch.bfloat16)
