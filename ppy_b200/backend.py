@@ -29,7 +29,7 @@ from ppy_compiler.backend import (
 from ppy_compiler.ir.passes import Pass, PassContext
 
 from . import __version__, artifacts
-from .passes import CommonTensorsToBuffers, ReductionsToTrailingAxes
+from .passes import CommonTensorsToBuffers, ReductionsToTrailingAxes, ThreadChunksToRanges
 from .scalar_c import Unsupported
 from .toolchain import ARCH, CSRC, nvcc, nvcc_version
 
@@ -87,6 +87,7 @@ class B200Backend(Backend):
     def register_passes(self, passes: BackendPassRegistrar) -> None:
         passes.add(CommonTensorsToBuffers)
         passes.add(ReductionsToTrailingAxes)
+        passes.add(ThreadChunksToRanges)
         passes.add(KernelPlanRemarks)
 
     def validate(self, module, context: BackendContext) -> None:

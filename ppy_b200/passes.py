@@ -19,7 +19,7 @@ buffer, and `role` in the manifest says whether the call reads it, writes it or 
 
 from __future__ import annotations
 
-from ppy_compiler.ir import BufferType, Builder, PtrType
+from ppy_compiler.ir import BufferType, Builder, PtrType, Successor
 from ppy_compiler.ir.dialects import core
 from ppy_compiler.ir.dialects import tensor as tensor_dialect
 from ppy_compiler.ir.passes import Pass, PassContext
@@ -27,7 +27,7 @@ from ppy_compiler.ir.passes import Pass, PassContext
 from .scalar_c import Unsupported
 
 __all__ = ["CommonTensorsToBuffers", "common_tensors_to_buffers", "ReductionsToTrailingAxes",
-           "reductions_to_trailing_axes"]
+           "reductions_to_trailing_axes", "ThreadChunksToRanges", "thread_chunks_to_ranges"]
 
 
 def _cast(value, dtype: str):
@@ -212,6 +212,105 @@ class ReductionsToTrailingAxes(Pass):
 
     def run(self, module, ctx: PassContext) -> bool:
         changed = reductions_to_trailing_axes(module)
+        if changed:
+            ctx.invalidate()
+        return changed
+
+
+# ---------------------------------------------------------------- thread chunks back into ranges
+
+
+def _is_float(t) -> bool:
+    return str(t).startswith(("f", "bf"))
+
+
+def _drop_unreachable(function) -> None:
+    blocks = function.body.blocks
+    reached, todo = set(), [blocks[0]]
+    while todo:
+        block = todo.pop()
+        if id(block) in reached:
+            continue
+        reached.add(id(block))
+        todo.extend(block.successors)
+    for block in [b for b in blocks if id(b) not in reached]:
+        for op in reversed(list(block.operations)):
+            op.erase()
+        blocks.remove(block)
+
+
+def thread_chunks_to_ranges(module) -> bool:
+    """Give a `parallel.range` loop that PPy's default `threads` route split into host-thread
+    chunks back its range. That route (lower_parallel.py:141-318) leaves, per loop, a branch on
+    the range's size between a serial block -- one call of the chunk body `@f__parN` over the
+    whole range, the initial accumulator last -- and a spawn block that calls it on eight
+    chunks with `concurrency.spawn` and folds their partials in order. The serial call has
+    the operands, in the order, of the `parallel.reduce` / `parallel.for` that the `openmp`
+    route keeps (parallel.py:562-610): it becomes that op (for a reduction, its kind from how
+    the spawn block combines the initial value, reassociating integers only, as the frontend
+    decides at ast_to_ir.py:4026), the branch goes to the serial block, and the spawn block
+    and the task wrappers nothing calls any more go. True if anything changed."""
+    changed = False
+    for function in list(module.functions.values()):
+        if function.is_declaration:
+            continue
+        for block in list(function.body.blocks):
+            if not block.operations:
+                continue
+            branch = block.operations[-1]
+            if branch.name != "core.cond_br" or len(branch.successors) != 2:
+                continue
+            serial, spawn = branch.successors[0].block, branch.successors[1].block
+            if not (serial.name.startswith("par.serial") and spawn.name.startswith("par.spawn")):
+                continue
+            calls = [op for op in serial.operations if op.name == "core.call"]
+            if len(calls) != 1 or not any(op.name == "concurrency.spawn"
+                                          for op in spawn.operations):
+                continue
+            call = calls[0]
+            body = module.functions.get(call.attributes["callee"].name)
+            if body is None or body.attributes.get("ppy.synthesized") != "parallel":
+                continue
+            b = Builder().before(call)
+            if call.results:
+                init = call.operands[-1]
+                combine = next((op.name for op in spawn.operations
+                                if op.name in ("core.add", "core.mul")
+                                and any(v is init for v in op.operands)), None)
+                if combine is None:
+                    continue
+                result = call.results[0]
+                reduce_op = b.create("parallel.reduce", tuple(call.operands), (result.type,),
+                                     {"callee": call.attributes["callee"],
+                                      "op": "add" if combine == "core.add" else "mul",
+                                      "reassociate": not _is_float(result.type)})
+                result.replace_all_uses_with(reduce_op.results[0])
+            else:
+                b.create("parallel.for", tuple(call.operands), (),
+                         {"callee": call.attributes["callee"]})
+            call.erase()
+            Builder().before(branch).create("core.br", (), (), successors=(Successor(serial),))
+            branch.erase()
+            _drop_unreachable(function)
+            changed = True
+    if changed:
+        called = {op.attributes["callee"].name for fn in module.functions.values()
+                  if not fn.is_declaration for op in fn.operations()
+                  if "callee" in op.attributes}
+        for name, fn in list(module.functions.items()):
+            if fn.attributes.get("ppy.synthesized") == "parallel.reduce" and name not in called:
+                del module.functions[name]
+    return changed
+
+
+class ThreadChunksToRanges(Pass):
+    """Backend-stage pass: `parallel.range` loops split into host-thread chunks by PPy's default
+    `threads` route become whole `parallel.*` ops again (see `thread_chunks_to_ranges`)."""
+
+    name = "b200-thread-chunks-to-ranges"
+
+    def run(self, module, ctx: PassContext) -> bool:
+        changed = thread_chunks_to_ranges(module)
         if changed:
             ctx.invalidate()
         return changed

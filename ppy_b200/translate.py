@@ -908,12 +908,14 @@ def _is_tensor_function(function) -> bool:
 
 
 def plan_module(module) -> P.ModulePlan:
-    """Plan every defined function of `module`, or raise `Unsupported`. The backend pass that
-    moves reduced middle axes last runs here too (it changes nothing the second time), for IR
-    that reaches the translator without the backend's passes (a `.ppyir` read directly)."""
-    from .passes import reductions_to_trailing_axes
+    """Plan every defined function of `module`, or raise `Unsupported`. The backend passes
+    that move reduced middle axes last and give thread-chunked ranges back their range run here
+    too (they change nothing the second time), for IR that reaches the translator without the
+    backend's passes (a `.ppyir` read directly)."""
+    from .passes import reductions_to_trailing_axes, thread_chunks_to_ranges
 
     reductions_to_trailing_axes(module)
+    thread_chunks_to_ranges(module)
     functions = []
     notes: list[str] = []
     bodies = set()

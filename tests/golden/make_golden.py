@@ -682,6 +682,19 @@ def golden_layernorm() -> None:
     write_ppyir(shared_passes(build_layernorm(), False), "gpt2_layernorm")
 
 
+def golden_collatz_threads(reference: Path) -> None:
+    """The same Collatz program as PPy's default `threads` route hands it to a backend:
+    each `parallel.range` already split into host-thread chunks (`concurrency.spawn`)."""
+    with tempfile.TemporaryDirectory() as tmp:
+        root = Path(tmp)
+        (root / "pyproject.toml").write_text('[project]\nname = "collatz"\nversion = "0"\n',
+                                             encoding="utf-8")
+        (root / "collatz.ppy").write_text(textwrap.dedent(COLLATZ), encoding="utf-8")
+        text = _ppy(reference, root, "emit", "ir", "collatz.ppy")
+        assert "concurrency.spawn" in text
+        (HERE / "collatz_threads.ppyir").write_text(text, encoding="utf-8")
+
+
 def golden_collatz(reference: Path) -> None:
     from ppy_compiler.ir import decode
 
@@ -748,7 +761,8 @@ def main() -> None:
     options = parser.parse_args()
     _setup(options.reference)
     if options.only:
-        globals()[f"golden_{options.only}"]()
+        make = globals()[f"golden_{options.only}"]
+        make(options.reference) if make.__code__.co_argcount else make()
         print("golden fixture written to", HERE)
         return
     golden_chain()
@@ -759,6 +773,7 @@ def main() -> None:
     golden_layernorm()
     golden_views()
     golden_collatz(options.reference)
+    golden_collatz_threads(options.reference)
     print("golden fixtures written to", HERE)
 
 

@@ -176,21 +176,42 @@ COLLATZ_SOURCE = textwrap.dedent("""
 """)
 
 
-def test_parallel_range_source_needs_the_ir_op_and_says_how(project):
-    """PPy source with ppy.parallel.range (examples/35_parallel_range): under the default
-    threads route the range arrives already split into host-thread chunks, which the backend
-    refuses naming the setting that keeps it whole; with that setting it builds a reduce
-    kernel."""
+def test_parallel_range_source_builds_on_both_routes(project):
+    """PPy source with ppy.parallel.range (examples/35_parallel_range). Under the default
+    threads route the range arrives split into host-thread chunks (`concurrency.spawn`); the
+    backend's pass gives the loop its range back (ppy_b200.passes.thread_chunks_to_ranges) and
+    builds the same reduce kernel as under the openmp setting, which keeps the range whole."""
     root, site = project
     (root / "collatz.ppy").write_text(COLLATZ_SOURCE)
-    done = _ppy(root, site, "build", "collatz.ppy", "--backend", "b200", "-o", "out")
-    assert done.returncode != 0
-    text = done.stdout + done.stderr
-    assert "E1802" in text and '[tool.ppy.parallel] backend = "openmp"' in text
-    with (root / "pyproject.toml").open("a") as f:
-        f.write('\n[tool.ppy.parallel]\nbackend = "openmp"\n')
-    done = _ppy(root, site, "build", "collatz.ppy", "--backend", "b200", "-o", "out")
-    assert done.returncode == 0, done.stdout + done.stderr
-    manifest = json.loads((root / "out" / "collatz.json").read_text())
-    kernels = {fn["name"]: fn["kernels"] for fn in manifest["functions"]}
-    assert kernels["collatz_collatz_sum"] == ["reduce"]
+    kernels = []
+    for route in ("threads", "openmp"):
+        if route == "openmp":
+            with (root / "pyproject.toml").open("a") as f:
+                f.write('\n[tool.ppy.parallel]\nbackend = "openmp"\n')
+        done = _ppy(root, site, "build", "collatz.ppy", "--backend", "b200", "-o", route)
+        assert done.returncode == 0, done.stdout + done.stderr
+        manifest = json.loads((root / route / "collatz.json").read_text())
+        kernels.append({fn["name"]: fn["kernels"] for fn in manifest["functions"]})
+    assert kernels[0] == kernels[1]
+    assert kernels[0]["collatz_collatz_sum"] == ["reduce"]
+
+
+def test_thread_chunks_become_the_range_again(ppy_compiler):
+    """The threads route's IR of the Collatz program (tests/golden/collatz_threads.ppyir):
+    after the pass no concurrency op is left, and each loop is the parallel op the openmp
+    route's IR (tests/golden/collatz.ppyir) has, with the same callee and reduction."""
+    from ppy_compiler.ir import read, verify
+
+    from ppy_b200.passes import thread_chunks_to_ranges
+
+    module = read(GOLDEN / "collatz_threads.ppyir")
+    assert thread_chunks_to_ranges(module)
+    assert not verify(module)
+    ops = [op for fn in module.functions.values() if not fn.is_declaration
+           for op in fn.operations()]
+    assert not [op for op in ops if op.dialect == "concurrency"]
+    got = sorted((op.name, op.attributes["callee"].name, str(op.attributes.get("op")))
+                 for op in ops if op.dialect == "parallel")
+    assert got == [("parallel.for", "collatz_collatz_steps__par2", "None"),
+                   ("parallel.reduce", "collatz_collatz_sum__par1", "add")]
+    assert not thread_chunks_to_ranges(module)  # nothing left to do

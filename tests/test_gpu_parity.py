@@ -256,6 +256,21 @@ def test_collatz_steps_parallel_for_writes_device_memory(rt):
     assert np.array_equal(steps, oracle.collatz_steps(1, 4096)[1])
 
 
+def test_collatz_from_the_threads_route_matches_ppy_run(rt):
+    """The same program as PPy's default `threads` route hands it over -- each range split into
+    host-thread chunks (tests/golden/collatz_threads.ppyir) -- built after the backend gives
+    the chunks back their range: the reference's `ppy run` answers, bit for bit."""
+    module = rt.load(PREBUILT / "collatz_threads" / "collatz.json")
+    g = json.loads((GOLDEN / "collatz.json").read_text())
+    assert tuple(module.collatz_collatz_sum(1, 1 << 16)) == (0, g["sum_1_65536"])
+    assert tuple(module.collatz_collatz_sum(27, 28)) == (0, g["sum_27_28"])
+    assert tuple(module.collatz_collatz_sum(5, 5)) == (0, g["sum_5_5"])
+    out = torch.zeros(4095, dtype=torch.int64, device="cuda")
+    status, count = module.collatz_collatz_steps(out, 1, 4096)
+    assert (status, count) == (0, g["steps_count_1_4096"])
+    assert np.array_equal(out.cpu().numpy(), oracle.collatz_steps(1, 4096)[1])
+
+
 def test_collatz_large_range_against_the_oracle(rt):
     module = _load(rt, "collatz")
     hi = 1 << 24
