@@ -477,7 +477,7 @@ class Gpt2(Workload):
         self.dids = self.ids.cuda()
         self.pids = self.ids.pin_memory()
         b = self.ids.shape[0]
-        self.logits = torch.empty(b, self.LENGTH, 50257, device="cuda")
+        self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
         self.last = torch.empty(b, 50257).pin_memory()
 
     def step_device(self):
@@ -568,7 +568,7 @@ class Gpt2TP(Gpt2):
         self.pids = self.ids.pin_memory()
         v0, v1 = self.model.shard.vocab
         b = self.ids.shape[0]
-        self.logits = torch.empty(b, self.LENGTH, v1 - v0, device="cuda")
+        self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
         self.last = torch.empty(b, v1 - v0).pin_memory()
 
     def h2d_d2h(self):

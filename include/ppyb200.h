@@ -125,6 +125,13 @@ int32_t ppyb200_matmul_bf16(const uint16_t *a, const uint16_t *b, const float *b
 int32_t ppyb200_matmul_bf16_kmajor(const uint16_t *a, const uint16_t *bt, const float *bias,
                                    float *c, int64_t m, int64_t n, int64_t k);
 
+/* ppyb200_matmul_bf16_kmajor into rows `ldc` floats apart (ldc >= N): C[i*ldc + j] for
+ * j < N, nothing written in the columns N .. ldc-1 of a row. Rows that start on 128-byte
+ * lines (C 128-byte aligned, ldc % 32 == 0) store whole lines: GPT-2's logits, 50257 floats a
+ * row, go into rows 50272 apart. PPYB200_RAISED for ldc < N. */
+int32_t ppyb200_matmul_bf16_kmajor_ld(const uint16_t *a, const uint16_t *bt, const float *bias,
+                                      float *c, int64_t ldc, int64_t m, int64_t n, int64_t k);
+
 /* bt[n*K + k] = b[k*N + n]: a bf16 [K,N] matrix into [N,K] (tiled through shared memory). */
 int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64_t n);
 

@@ -45,10 +45,10 @@ int32_t ppyb200_transpose_bf16(const uint16_t* b, uint16_t* bt, int64_t k, int64
   return finish(e, "ppyb200_transpose_bf16", 1);
 }
 
-int32_t ppyb200_matmul_bf16_kmajor(const uint16_t* a, const uint16_t* bt, const float* bias,
-                                   float* c, int64_t m, int64_t n, int64_t k) {
-  if (m < 0 || n < 0 || k < 0) {
-    ppyb200_set_error("ppyb200_matmul_bf16_kmajor: negative extent");
+int32_t ppyb200_matmul_bf16_kmajor_ld(const uint16_t* a, const uint16_t* bt, const float* bias,
+                                      float* c, int64_t ldc, int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k < 0 || ldc < n) {
+    ppyb200_set_error("ppyb200_matmul_bf16_kmajor_ld: extents >= 0 and ldc >= N");
     return PPYB200_RAISED;
   }
   if (m == 0 || n == 0) return PPYB200_OK;
@@ -60,13 +60,33 @@ int32_t ppyb200_matmul_bf16_kmajor(const uint16_t* a, const uint16_t* bt, const 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(ppyb200_stream());
   int32_t* status = ppyb200_status_word();
   if (status == nullptr) return PPYB200_RAISED;
-  // C = A.B + bias by columns of 32 rows (measured faster here than the four-column form
-  // whenever the rows allow either: 0.80 against 0.85 ms at 8192^3)
-  cudaError_t e = ppyb200::gemm::launch(reinterpret_cast<const __nv_bfloat16*>(a),
-                                        reinterpret_cast<const __nv_bfloat16*>(bt), m, n, k,
-                                        ppyb200::gemm::BiasEpilogue{bias, c, n}, status,
-                                        ppyb200_sm_count(), stream);
+  // Deep K (the MMAs set the pace): C = A.B + bias by columns of 32 rows, each store 32
+  // consecutive floats of one row (0.806 against 0.826 ms for quads at 8192^3). Shallow K
+  // (the stores set it): four-column quads, a quarter of the store instructions, on CTA
+  // pairs, which halve each SM's operand loads once the stores no longer bound the tile
+  // (GPT-2's LM head, 32768 x 50257 x 768 into rows 50272 apart: 2.48 ms, against 2.79 for
+  // quads on one CTA per tile and 2.92 for columns). Either form stores whole 128-byte lines
+  // when rows start on one (C aligned so, ldc % 32 == 0) and splits every store over two
+  // lines otherwise (3.08 ms with ldc = 50257). PPYB200_GEMM_SINGLE keeps one CTA per tile.
+  const auto* A = reinterpret_cast<const __nv_bfloat16*>(a);
+  const auto* B = reinterpret_cast<const __nv_bfloat16*>(bt);
+  cudaError_t e;
+  if (k < ppyb200::gemm::PAIR_MIN_K && ldc % 4 == 0 && aligned16(c) &&
+      (bias == nullptr || aligned16(bias))) {
+    const ppyb200::gemm::BiasQuads epi{bias, c, ldc, n};
+    if (ppyb200_gemm_form() == PPYB200_GEMM_SINGLE)
+      e = ppyb200::gemm::launch_single(A, B, m, n, k, epi, status, ppyb200_sm_count(), stream);
+    else
+      e = ppyb200::gemm::launch_pair(A, B, m, n, k, epi, status, stream);
+  } else
+    e = ppyb200::gemm::launch(A, B, m, n, k, ppyb200::gemm::BiasEpilogue{bias, c, ldc}, status,
+                              ppyb200_sm_count(), stream);
   return finish(e, "ppyb200_matmul_bf16_kmajor", 1);
+}
+
+int32_t ppyb200_matmul_bf16_kmajor(const uint16_t* a, const uint16_t* bt, const float* bias,
+                                   float* c, int64_t m, int64_t n, int64_t k) {
+  return ppyb200_matmul_bf16_kmajor_ld(a, bt, bias, c, n, m, n, k);
 }
 
 int32_t ppyb200_matmul_bf16(const uint16_t* a, const uint16_t* b, const float* bias, float* c,

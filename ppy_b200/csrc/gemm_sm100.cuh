@@ -261,6 +261,39 @@ struct BiasEpilogue {
   }
 };
 
+// C = A.B + bias by four-column quads: eight lanes store one row's 32 consecutive floats as
+// float4s, four rows per instruction, so rows that start on 128-byte lines take whole lines
+// at a quarter of the column form's store instructions. c and bias 16-byte aligned, ldc % 4
+// == 0; a quad that crosses N stores its columns below N one at a time.
+struct BiasQuads {
+  static constexpr bool kQuads = true;
+  const float* bias;
+  float* c;
+  int64_t ldc;
+  int64_t n;
+  __device__ __forceinline__ void store_quads(const float4 (&v)[8], int64_t row, int count,
+                                              int64_t col) const {
+    float* p = c + row * ldc + col;
+    if (col + 4 <= n) {
+      const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < count)
+          __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc),
+                 make_float4(v[i].x + b.x, v[i].y + b.y, v[i].z + b.z, v[i].w + b.w));
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i >= count) break;
+      const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      for (int j = 0; j < 4 && col + j < n; ++j)
+        __stcs(p + 4 * i * ldc + j, bias != nullptr ? e[j] + __ldg(bias + col + j) : e[j]);
+    }
+  }
+};
+
 
 // One accumulator tile's epilogue for one warp: the 32 rows of its lane quarter (from row0,
 // `rows` of them inside C), the half of the BN columns from col0 + half * BN / 2; `acc` is the

@@ -61,9 +61,11 @@ def _bind(lib) -> None:
     lib.ppyb200_attention_causal_bf16.argtypes = [p, p, i64, i64, i64, i64]
     lib.ppyb200_attention_causal_vt_bf16.argtypes = [p, p, p, i64, i64, i64, i64, p]
     lib.ppyb200_matmul_bf16_kmajor.argtypes = [p, p, p, p, i64, i64, i64]
+    lib.ppyb200_matmul_bf16_kmajor_ld.argtypes = [p, p, p, p, i64, i64, i64, i64]
     for name in ("ppyb200_gpt2_embed", "ppyb200_linear_bf16", "ppyb200_linear_residual",
                  "ppyb200_linear_qkv_bf16", "ppyb200_attention_causal_bf16",
-                 "ppyb200_attention_causal_vt_bf16", "ppyb200_matmul_bf16_kmajor"):
+                 "ppyb200_attention_causal_vt_bf16", "ppyb200_matmul_bf16_kmajor",
+                 "ppyb200_matmul_bf16_kmajor_ld"):
         getattr(lib, name).restype = i32
     lib._gpt2_bound = True
 
@@ -129,10 +131,36 @@ class GPT2:
         if status != runtime.STATUS_OK:
             raise runtime.B200Error(f"{what}: {runtime.last_error()}")
 
-    def forward(self, ids, logits=None):
-        """Logits [batch, length, vocab] (f32) for token ids [batch, length] (int64, CUDA)."""
+    def new_logits(self, batch: int, length: int):
+        """An f32 [batch, length, vocab] tensor whose rows start on 128-byte lines: a view of
+        [batch, length, vocab rounded up to 32] (50272 for 50257), so that the LM head stores
+        whole lines (a 50257-float row starts anywhere in a line and splits every store over
+        two). Values live in the first `vocab` columns only."""
         import torch
 
+        v = self.config.vocab
+        pitch = (v + 31) // 32 * 32
+        rows = torch.empty(batch, length, pitch, dtype=torch.float32, device=self.device)
+        return rows[:, :, :v]
+
+    @staticmethod
+    def _row_pitch(logits, batch: int, length: int, vocab: int) -> int:
+        """The distance between consecutive logits rows, in floats, of a [batch, length, vocab]
+        f32 tensor whose rows are evenly spaced (contiguous, or a view such as new_logits)."""
+        import torch
+
+        if (tuple(logits.shape) != (batch, length, vocab) or logits.dtype != torch.float32
+                or logits.device.type != "cuda" or logits.stride(2) != 1):
+            raise runtime.B200Error(f"logits: f32 [{batch}, {length}, {vocab}] on the GPU, "
+                                    "unit stride along the vocabulary")
+        pitch = logits.stride(1)
+        if pitch < vocab or (batch > 1 and logits.stride(0) != length * pitch):
+            raise runtime.B200Error("logits: rows evenly spaced, at least vocab floats apart")
+        return pitch
+
+    def forward(self, ids, logits=None):
+        """Logits [batch, length, vocab] (f32) for token ids [batch, length] (int64, CUDA),
+        into `logits` when given (any evenly spaced rows), else into new_logits()."""
         cfg = self.config
         batch, length = ids.shape
         tokens = batch * length
@@ -144,7 +172,8 @@ class GPT2:
         x, h, qkv, vt, att, f = s["x"], s["h"], s["qkv"], s["vt"], s["att"], s["f"]
         status = s["status"]
         if logits is None:
-            logits = torch.empty(batch, length, v, dtype=torch.float32, device=self.device)
+            logits = self.new_logits(batch, length)
+        pitch = self._row_pitch(logits, batch, length, v)
         lib = self.lib
         st = status.data_ptr()
         status.zero_()
@@ -173,8 +202,9 @@ class GPT2:
                                                     blk["b_proj"].data_ptr(), x.data_ptr(),
                                                     tokens, c, 4 * c, st), "proj")
         self._check(ln(x, self.lnf_g, self.lnf_b, h).status, "layernorm")
-        self._check(lib.ppyb200_matmul_bf16_kmajor(h.data_ptr(), self.wte.data_ptr(), None,
-                                                   logits.data_ptr(), tokens, v, c), "lm head")
+        self._check(lib.ppyb200_matmul_bf16_kmajor_ld(h.data_ptr(), self.wte.data_ptr(), None,
+                                                      logits.data_ptr(), pitch, tokens, v, c),
+                    "lm head")
         return logits
 
     def profile(self, ids, logits=None) -> dict:
@@ -208,7 +238,7 @@ class GPT2:
 
         names = {"ppyb200_gpt2_embed": "embed", "ppyb200_linear_qkv_bf16": "qkv",
                  "ppyb200_attention_causal_vt_bf16": "attention",
-                 "ppyb200_matmul_bf16_kmajor": "lm_head"}
+                 "ppyb200_matmul_bf16_kmajor_ld": "lm_head"}
         for symbol, name in names.items():
             original[symbol] = getattr(lib, symbol)
         linear = lib.ppyb200_linear_bf16

@@ -295,10 +295,19 @@ class GPT2TensorParallel:
         if self.shard.size > 1:
             dist.all_reduce(x, group=self.group)
 
-    def forward(self, ids, logits=None):
-        """This rank's logits [batch, length, v1 - v0] (f32) for the vocab rows [v0, v1)."""
+    def new_logits(self, batch: int, length: int):
+        """This rank's f32 [batch, length, v1 - v0] logits with rows on 128-byte lines (the
+        row pitch rounded up to 32 floats), as GPT2.new_logits."""
         import torch
 
+        v0, v1 = self.shard.vocab
+        pitch = (v1 - v0 + 31) // 32 * 32
+        rows = torch.empty(batch, length, pitch, dtype=torch.float32, device="cuda")
+        return rows[:, :, :v1 - v0]
+
+    def forward(self, ids, logits=None):
+        """This rank's logits [batch, length, v1 - v0] (f32) for the vocab rows [v0, v1),
+        into `logits` when given (any evenly spaced rows), else into new_logits()."""
         cfg = self.config
         batch, length = ids.shape
         tokens = batch * length
@@ -314,7 +323,8 @@ class GPT2TensorParallel:
         x, h, qkv, vt, att, f = s["x"], s["h"], s["qkv"], s["vt"], s["att"], s["f"]
         status = s["status"]
         if logits is None:
-            logits = torch.empty(batch, length, v1 - v0, dtype=torch.float32, device="cuda")
+            logits = self.new_logits(batch, length)
+        pitch = GPT2._row_pitch(logits, batch, length, v1 - v0)
         lib = self.lib
         st = status.data_ptr()
         status.zero_()
@@ -338,9 +348,9 @@ class GPT2TensorParallel:
                                                 c, 1, st), "fc")
             self._row_parallel(f, blk["w_proj"], blk["b_proj"], x, tokens, fl, st, "proj")
         self._check(ln(x, self.lnf_g, self.lnf_b, h).status, "layernorm")
-        self._check(lib.ppyb200_matmul_bf16_kmajor(h.data_ptr(), self.head.data_ptr(), None,
-                                                   logits.data_ptr(), tokens, v1 - v0, c),
-                    "lm head")
+        self._check(lib.ppyb200_matmul_bf16_kmajor_ld(h.data_ptr(), self.head.data_ptr(), None,
+                                                      logits.data_ptr(), pitch, tokens, v1 - v0,
+                                                      c), "lm head")
         return logits
 
     def status(self) -> int:

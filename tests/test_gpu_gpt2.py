@@ -210,6 +210,31 @@ def test_small_gpt2_forward_matches_torch(lib):
     _close_logits(logits, ref)
 
 
+def test_logits_rows_on_lines_or_contiguous(lib):
+    """The default logits (a view of rows 50272 floats apart) and a caller's contiguous
+    [batch, length, 50257] buffer hold the same values bit for bit; a caller's padded rows
+    keep their padding; unevenly spaced rows are refused."""
+    from ppy_b200 import runtime
+    from ppy_b200.gpt2 import GPT2, Config
+
+    model = GPT2(Config(layers=1), seed=1)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    ids = torch.randint(0, 50257, (2, 128), device="cuda", generator=g)
+    lined = model.forward(ids)
+    assert lined.shape == (2, 128, 50257) and lined.stride() == (128 * 50272, 50272, 1)
+    dense = torch.empty(2, 128, 50257, device="cuda")
+    assert model.forward(ids, dense) is dense
+    padded = torch.full((2, 128, 50300), 7.0, device="cuda")
+    model.forward(ids, padded[:, :, :50257])
+    torch.cuda.synchronize()
+    assert model.status() == 0
+    assert torch.equal(lined, dense) and torch.equal(padded[:, :, :50257], dense)
+    assert torch.all(padded[:, :, 50257:] == 7.0)
+    uneven = torch.empty(2, 130, 50272, device="cuda")[:, :128, :50257]
+    with pytest.raises(runtime.B200Error):
+        model.forward(ids, uneven)
+
+
 def test_gpt2_124m_forward_matches_torch(lib):
     from ppy_b200.gpt2 import GPT2, GPT2_124M
 

@@ -27,6 +27,8 @@ def lib():
     for name in ("ppyb200_matmul_bf16", "ppyb200_matmul_bf16_kmajor"):
         getattr(lib, name).argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
         getattr(lib, name).restype = ctypes.c_int32
+    lib.ppyb200_matmul_bf16_kmajor_ld.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4
+    lib.ppyb200_matmul_bf16_kmajor_ld.restype = ctypes.c_int32
     lib.ppyb200_transpose_bf16.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                            ctypes.c_int64]
     lib.ppyb200_set_gemm_form.argtypes = [ctypes.c_int32]
@@ -149,6 +151,33 @@ def test_logit_rows_at_any_offset(lib, offset):
     torch.cuda.synchronize()
     _check(out, _reference(a, b, bias), rel=1e-4)
     assert torch.all(buf[:offset] == 7.0) and torch.all(buf[offset + m * n:] == 7.0)
+
+
+@pytest.mark.parametrize("m,n,k,ldc", [(260, 50257, 128, 50272), (300, 520, 192, 544),
+                                        (256, 256, 64, 257), (130, 131, 128, 131)])
+def test_rows_at_a_pitch(lib, m, n, k, ldc):
+    """C in rows ldc floats apart: the values of the contiguous call, bit for bit, and the
+    columns N .. ldc-1 of every row untouched (128-byte lines, odd pitches, ldc == N)."""
+    a, b, bias = _operands(m, n, k, seed=10)
+    da, dbt, dbias = a.cuda(), b.t().contiguous().cuda(), bias.cuda()
+    rows = torch.full((m + 1, ldc), 7.0, device="cuda")
+    dense = torch.empty((m, n), device="cuda")
+    assert lib.ppyb200_matmul_bf16_kmajor_ld(_ptr(da), _ptr(dbt), _ptr(dbias), _ptr(rows), ldc,
+                                             m, n, k) == 0
+    assert lib.ppyb200_matmul_bf16_kmajor(_ptr(da), _ptr(dbt), _ptr(dbias), _ptr(dense), m, n,
+                                          k) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(rows[:m, :n], dense)
+    assert torch.all(rows[:m, n:] == 7.0) and torch.all(rows[m] == 7.0)
+    _check(dense, _reference(a, b, bias), rel=1e-4)
+
+
+def test_pitch_below_n_is_refused(lib):
+    a = torch.zeros(128, 64, dtype=torch.bfloat16, device="cuda")
+    bt = torch.zeros(256, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(128, 256, device="cuda")
+    assert lib.ppyb200_matmul_bf16_kmajor_ld(_ptr(a), _ptr(bt), None, _ptr(out), 255, 128, 256,
+                                             64) == -1
 
 
 @pytest.mark.parametrize("m,n,k", [(100, 70, 33), (1, 256, 64), (129, 257, 65)])
