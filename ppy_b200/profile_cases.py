@@ -5,7 +5,8 @@ one launch of it alone.
     python -m ppy_b200.profile_cases gemm        # matmul_bf16_kernel, 8192^3, K-major B
     python -m ppy_b200.profile_cases attention   # causal_kernel, batch 32 x 1024, 12 heads
     python -m ppy_b200.profile_cases fc          # matmul_bf16_kernel, GELU epilogue, GPT-2 FC
-    python -m ppy_b200.profile_cases lm_head     # matmul_bf16_kernel, N = 50257 logits
+    python -m ppy_b200.profile_cases lm_head     # matmul_bf16_pair_kernel, quads epilogue,
+                                                 # 50257 logits a row in rows 50272 apart
 
 Each case launches its kernel three times (two warm-ups, then the one to capture: `-s 2`).
 """
@@ -38,10 +39,12 @@ def main() -> None:
         if case in ("gemm", "lm_head"):
             if not hasattr(main, "operands"):
                 m, n, k = (8192, 8192, 8192) if case == "gemm" else (4096, 50257, 768)
-                main.operands = (rand(m, k), rand(n, k), torch.empty(m, n, device="cuda"), m, n, k)
-            a, bt, c, m, n, k = main.operands
-            status = lib.ppyb200_matmul_bf16_kmajor(a.data_ptr(), bt.data_ptr(), None,
-                                                    c.data_ptr(), m, n, k)
+                ldc = n if case == "gemm" else 50272  # the GPT-2 forward's logits rows
+                main.operands = (rand(m, k), rand(n, k), torch.empty(m, ldc, device="cuda"),
+                                 ldc, m, n, k)
+            a, bt, c, ldc, m, n, k = main.operands
+            status = lib.ppyb200_matmul_bf16_kmajor_ld(a.data_ptr(), bt.data_ptr(), None,
+                                                       c.data_ptr(), ldc, m, n, k)
         elif case == "attention":
             if not hasattr(main, "operands"):
                 main.operands = (rand(32 * 1024, 3 * 768), rand(32 * 12 * 64, 1024),

@@ -153,11 +153,13 @@ def test_logit_rows_at_any_offset(lib, offset):
     assert torch.all(buf[:offset] == 7.0) and torch.all(buf[offset + m * n:] == 7.0)
 
 
-@pytest.mark.parametrize("m,n,k,ldc", [(260, 50257, 128, 50272), (300, 520, 192, 544),
+@pytest.mark.parametrize("m,n,k,ldc", [(260, 50257, 128, 50272), (260, 25129, 768, 25152),
+                                        (300, 520, 192, 544),
                                         (256, 256, 64, 257), (130, 131, 128, 131)])
 def test_rows_at_a_pitch(lib, m, n, k, ldc):
     """C in rows ldc floats apart: the values of the contiguous call, bit for bit, and the
-    columns N .. ldc-1 of every row untouched (128-byte lines, odd pitches, ldc == N)."""
+    columns N .. ldc-1 of every row untouched (128-byte lines -- the LM head's 50257 and a
+    two-rank vocabulary slice's 25129 -- odd pitches, ldc == N)."""
     a, b, bias = _operands(m, n, k, seed=10)
     da, dbt, dbias = a.cuda(), b.t().contiguous().cuda(), bias.cuda()
     rows = torch.full((m + 1, ldc), 7.0, device="cuda")

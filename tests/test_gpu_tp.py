@@ -1,5 +1,6 @@
 """The tensor-parallel GPT-2 forward (ppy_b200.gpt2_tp) on 2, 4 and 8 GPUs, one process each --
-one group of 2, two data-parallel groups of 2, one group of 4, two groups of 4 -- with the
+one group of 2, two data-parallel groups of 2, one group of 4, two groups of 4, and a group of
+one on a single GPU (the whole vocabulary in one rank's pitched logits rows) -- with the
 row-parallel exchange over NCCL or fused into the GEMM over NVLink: every rank's logits slice
 of its group's sequences against the torch float32 forward of the same weights (the
 reference's ATen block, examples/46_gpt2/gpt2.ppy:18-57) and against the one-GPU forward of
@@ -68,7 +69,7 @@ def _rank(rank: int, world: int, port: int, queue, tp: int = 0, exchange: str = 
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,tp,exchange", [(2, 0, "nccl"), (2, 0, "nvlink"),
+@pytest.mark.parametrize("world,tp,exchange", [(1, 0, "nccl"), (2, 0, "nccl"), (2, 0, "nvlink"),
                                                (4, 2, "nccl"), (4, 2, "nvlink"),
                                                (4, 0, "nvlink"), (8, 0, "nccl")])
 def test_tensor_parallel_forward(world, tp, exchange):
