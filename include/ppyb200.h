@@ -137,7 +137,7 @@ int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64
 
 /* Which tensor-core GEMM kernel every bf16 matmul of this library launches (the matmul entry
  * points, the GPT-2 linear layers, built modules' matmuls): PPYB200_GEMM_BY_SHAPE (the
- * default) clusters of two CTAs per 256 x 256 tile (tcgen05.mma.cta_group::2) when K >= 2048
+ * default) clusters of two CTAs per 256 x 256 tile (tcgen05.mma.cta_group::2) when M >= 256
  * and one CTA per 128 x 256 tile otherwise; PPYB200_GEMM_PAIRS and PPYB200_GEMM_SINGLE one of
  * them always. Process-wide; returns the previous form, or PPYB200_RAISED for another value. */
 #define PPYB200_GEMM_BY_SHAPE 0

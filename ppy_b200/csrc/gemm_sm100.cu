@@ -71,7 +71,7 @@ int32_t ppyb200_matmul_bf16_kmajor_ld(const uint16_t* a, const uint16_t* bt, con
   const auto* A = reinterpret_cast<const __nv_bfloat16*>(a);
   const auto* B = reinterpret_cast<const __nv_bfloat16*>(bt);
   cudaError_t e;
-  if (k < ppyb200::gemm::PAIR_MIN_K && ldc % 4 == 0 && aligned16(c) &&
+  if (k < ppyb200::gemm::DEEP_K && ldc % 4 == 0 && aligned16(c) &&
       (bias == nullptr || aligned16(bias))) {
     const ppyb200::gemm::BiasQuads epi{bias, c, ldc, n};
     if (ppyb200_gemm_form() == PPYB200_GEMM_SINGLE)

@@ -850,10 +850,9 @@ inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt
 
 inline size_t pair_shared_bytes() { return sizeof(PairShared) + 1024; }
 
-// K from which CTA pairs run by default: with K = 3072 and 8192 they measured 3 % and 2.4 %
-// faster than one CTA per tile; at K = 768 (short loops whose epilogues set the pace) equal
-// or slower.
-constexpr int64_t PAIR_MIN_K = 2048;
+// K from which a tile's MMAs, not its stores, set its pace (C = A.B + bias keeps the column
+// form there: quads measured 2.5 % slower at 8192^3, and faster at K = 768).
+constexpr int64_t DEEP_K = 2048;
 
 
 // The 2-CTA kernel on `stream`: clusters of two CTAs, as many as can be resident at once (at
@@ -901,7 +900,12 @@ inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64
                           int64_t k, Epi epi, int32_t* status, int sm_count,
                           cudaStream_t stream) {
   const int32_t form = ppyb200_gemm_form();
-  if (form == PPYB200_GEMM_PAIRS || (form == PPYB200_GEMM_BY_SHAPE && k >= PAIR_MIN_K))
+  // By shape: CTA pairs from two row blocks up. They halve each SM's operand loads and, with
+  // the accumulator released at CTA scope, measured faster than one CTA per tile at every
+  // GPT-2 shape (32768 rows, K = 768: out projection 0.765 against 0.829 ms, QKV 1.32 against
+  // 1.35, FC 1.92 against 1.95 per forward; K = 3072 and 8192: 3 % and 2.4 %). Below 256
+  // rows half of each pair would idle.
+  if (form == PPYB200_GEMM_PAIRS || (form == PPYB200_GEMM_BY_SHAPE && m >= 2 * BM))
     return launch_pair(a, bt, m, n, k, epi, status, stream);
   return launch_single(a, bt, m, n, k, epi, status, sm_count, stream);
 }
