@@ -144,14 +144,15 @@ class GPT2:
         return rows[:, :, :v]
 
     @staticmethod
-    def _row_pitch(logits, batch: int, length: int, vocab: int) -> int:
+    def _row_pitch(logits, batch: int, length: int, vocab: int, device: str = "cuda") -> int:
         """The distance between consecutive logits rows, in floats, of a [batch, length, vocab]
-        f32 tensor whose rows are evenly spaced (contiguous, or a view such as new_logits)."""
+        f32 tensor on `device` whose rows are evenly spaced (contiguous, or a view such as
+        new_logits)."""
         import torch
 
         if (tuple(logits.shape) != (batch, length, vocab) or logits.dtype != torch.float32
-                or logits.device.type != "cuda" or logits.stride(2) != 1):
-            raise runtime.B200Error(f"logits: f32 [{batch}, {length}, {vocab}] on the GPU, "
+                or logits.device.type != device or logits.stride(2) != 1):
+            raise runtime.B200Error(f"logits: f32 [{batch}, {length}, {vocab}] on {device}, "
                                     "unit stride along the vocabulary")
         pitch = logits.stride(1)
         if pitch < vocab or (batch > 1 and logits.stride(0) != length * pitch):
