@@ -62,23 +62,19 @@ int32_t ppyb200_matmul_bf16_kmajor_ld(const uint16_t* a, const uint16_t* bt, con
   if (status == nullptr) return PPYB200_RAISED;
   // Deep K (the MMAs set the pace): C = A.B + bias by columns of 32 rows, each store 32
   // consecutive floats of one row (0.806 against 0.826 ms for quads at 8192^3). Shallow K
-  // (the stores set it): four-column quads, a quarter of the store instructions, on CTA
-  // pairs, which halve each SM's operand loads once the stores no longer bound the tile
-  // (GPT-2's LM head, 32768 x 50257 x 768 into rows 50272 apart: 2.48 ms, against 2.79 for
-  // quads on one CTA per tile and 2.92 for columns). Either form stores whole 128-byte lines
+  // (the stores set it): four-column quads, a quarter of the store instructions (GPT-2's LM
+  // head, 32768 x 50257 x 768 into rows 50272 apart, on CTA pairs: 2.48 ms against 2.99 for
+  // columns; on one CTA per tile 2.79 against 2.92). Either form stores whole 128-byte lines
   // when rows start on one (C aligned so, ldc % 32 == 0) and splits every store over two
-  // lines otherwise (3.08 ms with ldc = 50257). PPYB200_GEMM_SINGLE keeps one CTA per tile.
+  // lines otherwise (3.08 ms with ldc = 50257). `launch` picks CTA pairs or one CTA per tile.
   const auto* A = reinterpret_cast<const __nv_bfloat16*>(a);
   const auto* B = reinterpret_cast<const __nv_bfloat16*>(bt);
   cudaError_t e;
   if (k < ppyb200::gemm::DEEP_K && ldc % 4 == 0 && aligned16(c) &&
-      (bias == nullptr || aligned16(bias))) {
-    const ppyb200::gemm::BiasQuads epi{bias, c, ldc, n};
-    if (ppyb200_gemm_form() == PPYB200_GEMM_SINGLE)
-      e = ppyb200::gemm::launch_single(A, B, m, n, k, epi, status, ppyb200_sm_count(), stream);
-    else
-      e = ppyb200::gemm::launch_pair(A, B, m, n, k, epi, status, stream);
-  } else
+      (bias == nullptr || aligned16(bias)))
+    e = ppyb200::gemm::launch(A, B, m, n, k, ppyb200::gemm::BiasQuads{bias, c, ldc, n}, status,
+                              ppyb200_sm_count(), stream);
+  else
     e = ppyb200::gemm::launch(A, B, m, n, k, ppyb200::gemm::BiasEpilogue{bias, c, ldc}, status,
                               ppyb200_sm_count(), stream);
   return finish(e, "ppyb200_matmul_bf16_kmajor", 1);
