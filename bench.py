@@ -1,27 +1,34 @@
 """Benchmark of the B200 path: one JSON line per run.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gelu|rows|collatz]
-                    [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200|reference]
 
-A step is one pass of the hot path over one batch of seeded synthetic input:
+A step is one pass of the hot path over one batch of seeded synthetic input. The default
+workload is the GPT-2-124M forward, the model half of the headline metric; the fused-group
+half (the GELU chain and the softmax->layernorm row group) rides in the same line under
+"workloads", each with its own value, e2e, roofline and CPU baseline.
 
-* gelu    -- y = gelu_tanh(a*b + c) over three fp32 vectors of 2^24 elements (uniform
-             [-4, 4], seed 0): the fused elementwise group, through the module the b200
-             backend builds from tests/golden/gelu.ppyir. Metric: GB/s of algorithmic
-             traffic (16 B per element).
-* rows    -- softmax then layernorm over each row of an fp32 [65536, 1024] matrix
-             (N(0,1), seed 0; gamma ~ N(1, .02), beta ~ N(0, .02)): the row group built
-             from tests/golden/rows.ppyir. Metric: GB/s (8 B per element + gamma, beta).
-* collatz -- the step counts of every start in [1, 2^26) summed and maxed: the
-             parallel.reduce kernels built from tests/golden/collatz.ppyir. Metric:
-             Collatz steps per second.
+* gpt2     -- GPT-2-124M forward (12 layers, width 768, 12 heads, vocab 50257), N(0, 0.02)
+              bf16 weights from seed 0, batch 32 x 1024 token ids (seed 0), f32 logits out;
+              data-parallel over the GPUs (32/N sequences each). Metric: tokens/s of the job.
+              The forward is captured once into a CUDA graph and replayed each step.
+* gpt2_tp  -- the same forward tensor-parallel (groups of --tp GPUs, data-parallel groups).
+* gelu     -- y = gelu_tanh(a*b + c) over three fp32 vectors of 2^24 elements (uniform
+              [-4, 4], seed 0), the module the backend builds from tests/golden/gelu.ppyir.
+              Metric: GB/s of algorithmic traffic (16 B per element).
+* rows     -- softmax then layernorm over each row of an fp32 [65536, 1024] matrix (N(0,1),
+              seed 0; gamma ~ N(1, .02), beta ~ N(0, .02)), from tests/golden/rows.ppyir.
+              Metric: GB/s (8 B per element + gamma, beta).
+* collatz  -- the step counts of every start in [1, 2^26) summed and maxed (parallel.reduce
+              kernels from tests/golden/collatz.ppyir). Metric: Collatz steps/s.
+* gemm     -- C = A @ B + bias, bf16 A and B, f32 accumulate and C, 8192^3. TFLOP/s.
+* gemm_f32 -- the fp32-input variant, 4096^3 (three tf32 products on the tensor cores).
 
-`value` is device-timed (CUDA events, inputs resident in HBM); `e2e` is the same metric
-through the host-memory C-ABI entry point (pinned host buffers, H2D and D2H inside the
-timed region). With --gpus N under torchrun each rank runs its own batch (weak scaling)
-or its slice of the Collatz range (strong), the time is the max over ranks.
-`--impl reference` times the oracle's C restatement of the reference's CPU loops on the
-host cores instead (rank 0 only).
+`value` is device-timed (CUDA events on the launching stream, inputs resident in HBM, max
+over ranks); `e2e` is the same metric through the host-memory path: every step copies its
+inputs in from pinned host memory and its whole output back (GPT-2: all logits).
+`--impl reference` times the CPU implementation of the path on the host cores instead
+(rank 0 only): the oracle's C restatement of the reference's CPU loops, and for GPT-2 the
+reference's own path, torch ATen, on the CPU.
 """
 
 from __future__ import annotations
@@ -44,21 +51,28 @@ PREBUILT = REPO / "ppy_b200" / "prebuilt"
 GELU_N = 1 << 24
 ROWS, COLS = 65536, 1024
 COLLATZ_HI = 1 << 26
+VOCAB = 50257
 
 
 def _args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--workload", default="gelu",
-                   choices=["gelu", "rows", "collatz", "gemm", "gpt2", "gpt2_tp"])
+    p.add_argument("--workload", default="gpt2",
+                   choices=["gpt2", "gpt2_tp", "gelu", "rows", "collatz", "gemm", "gemm_f32"])
+    p.add_argument("--extras", default="gelu,rows",
+                   help="with the gpt2 workload: the fused-group workloads measured in the same "
+                        "run and reported under 'workloads' ('none' for none)")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--tp", type=int, default=0,
                    help="gpt2_tp: ranks per tensor-parallel group (0: the widest that fits)")
     p.add_argument("--exchange", default="nvlink", choices=["nvlink", "nccl"],
                    help="gpt2_tp: the row-parallel sum fused into the GEMM over NVLink, or "
                         "an NCCL all-reduce after it")
+    p.add_argument("--eager", action="store_true",
+                   help="gpt2: launch the forward's kernels one by one instead of replaying a "
+                        "CUDA graph")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU-baseline sample length (seconds of host work)")
     return p.parse_args()
@@ -138,7 +152,8 @@ class Dist:
 
 
 class Clocks:
-    """nvidia-smi samples every 20 ms (SM clock, throttle reasons) around the timed region."""
+    """nvidia-smi samples every 20 ms (SM clock, throttle reasons); summarised over the
+    timed regions marked with `mark`."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -147,7 +162,7 @@ class Clocks:
     def __init__(self, device: int) -> None:
         self.device = device
         self.samples: list[tuple[float, list[str]]] = []
-        self.window: tuple[float, float] | None = None
+        self.windows: list[tuple[float, float]] = []
         self.process = None
         self._thread = threading.Thread(target=self._read, daemon=True)
 
@@ -168,9 +183,9 @@ class Clocks:
             self.process = None
 
     def mark(self, begin: float, end: float) -> None:
-        self.window = (begin, end)
+        self.windows.append((begin, end))
 
-    def stop(self) -> dict:
+    def stop(self) -> None:
         if self.process is not None:
             time.sleep(0.05)
             self.process.terminate()
@@ -179,10 +194,13 @@ class Clocks:
             except subprocess.TimeoutExpired:
                 self.process.kill()
             self._thread.join(timeout=5)
+
+    def summary(self, windows=None) -> dict:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        windows = self.windows if windows is None else windows
         inside = [s for t, s in self.samples
-                  if self.window and self.window[0] - 0.02 <= t <= self.window[1] + 0.02]
+                  if any(b - 0.02 <= t <= e + 0.02 for b, e in windows)]
         chosen = inside or [s for _, s in self.samples]
 
         def number(text):
@@ -203,12 +221,15 @@ class Clocks:
                 "samples": len(chosen), "samples_in_timed_region": len(inside)}
 
 
-def peaks() -> dict:
+def measured_peaks() -> dict:
+    """The pool's measured peaks, else the fallback figures (said so in `source`)."""
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return {"hbm_gbs": data["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
+                "bf16_tflops_sustained": data["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
 
 
 def traffic(kernel: str) -> float | None:
@@ -216,8 +237,7 @@ def traffic(kernel: str) -> float | None:
     path = REPO / "profiles" / "traffic.json"
     if not path.exists():
         return None
-    data = json.loads(path.read_text())
-    entry = data.get(kernel)
+    entry = json.loads(path.read_text()).get(kernel)
     return float(entry["bytes_per_launch"]) if entry else None
 
 
@@ -225,29 +245,52 @@ def traffic(kernel: str) -> float | None:
 
 
 class Workload:
+    name = ""
     metric = ""
     unit = ""
     dtype = ""
     kernel = ""
     scaling = "weak"
+    sample = ""
 
     def __init__(self, dist: Dist) -> None:
         self.dist = dist
+        self.tp = 0
+        self.exchange = "nvlink"
+        self.eager = False
+
+    def units(self) -> float:
+        """Units of the metric one step of this rank processes."""
+        return float(self.bytes_per_step)
+
+    def job_units(self) -> float:
+        """Units of the metric one step of the whole job processes."""
+        return self.units() * (self.dist.world if self.scaling == "weak" else 1)
+
+    def roofline(self, kernel_ms: float, peaks: dict) -> dict:
+        achieved = self.bytes_per_step / (kernel_ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic(self.kernel),
+                "peak_source": f"{peaks['source']} HBM copy", "kernel": self.kernel,
+                "kernel_ms": kernel_ms,
+                "algorithmic_bytes_per_launch": self.bytes_per_step}
 
 
 class Gelu(Workload):
+    name = "gelu_chain_f32"
     metric = "fused-group GB/s: y = gelu_tanh(a*b + c), fp32, 2^24 elements"
     unit = "GB/s"
     dtype = "f32"
     kernel = "gelu_chain_k0_v"
     bytes_per_step = 16 * GELU_N
+    sample = "the first 2^22 elements of the batch, repeated"
 
     def inputs(self):
         rng = np.random.default_rng(0 + self.dist.rank)
         self.host = [rng.uniform(-4, 4, GELU_N).astype(np.float32) for _ in range(3)]
 
     def config(self):
-        return {"workload": "gelu_chain_f32", "elements": GELU_N, "seed": 0,
+        return {"workload": self.name, "elements": GELU_N, "seed": 0,
                 "bytes_per_step": self.bytes_per_step,
                 "l2": "inputs larger than L2 (201 MB read per step), no flush"}
 
@@ -267,27 +310,26 @@ class Gelu(Workload):
     def h2d_d2h(self):
         return 12 * GELU_N, 4 * GELU_N
 
-    def cpu_step(self, threads: int, oracle):
-        # a bounded sample of the batch: the first 2^22 elements
+    def cpu_step(self, threads: int, oracle) -> float:
         n = 1 << 22
-        oracle.gelu_chain(self.host[0][:n], self.host[1][:n], self.host[2][:n], threads=threads)
-        return 16 * n
+        self.cpu_out = oracle.gelu_chain(self.host[0][:n], self.host[1][:n], self.host[2][:n],
+                                         threads=threads)
+        return 16.0 * n
 
-    def check(self, oracle):
-        sample = slice(0, 1 << 16)
-        expected = oracle.gelu_chain(self.host[0][sample].copy(), self.host[1][sample].copy(),
-                                     self.host[2][sample].copy())
-        got = self.out[: 1 << 16].cpu().numpy()
-        scale = np.maximum(np.abs(expected), 1.0)
-        return float(np.max(np.abs(got - expected) / scale))
+    def compare(self) -> float:
+        """Max scaled error of the device output against the oracle's on the CPU sample."""
+        got = self.out[: self.cpu_out.size].cpu().numpy()
+        return float(np.max(np.abs(got - self.cpu_out) / np.maximum(np.abs(self.cpu_out), 1.0)))
 
 
 class Rows(Workload):
+    name = "softmax_layernorm_rows_f32"
     metric = "fused-group GB/s: row softmax -> layernorm, fp32 [65536, 1024]"
     unit = "GB/s"
     dtype = "f32"
     kernel = "softmax_layernorm_k0"
     bytes_per_step = 2 * 4 * ROWS * COLS + 2 * 4 * COLS
+    sample = "the first 4096 rows of the batch, repeated"
 
     def inputs(self):
         rng = np.random.default_rng(0 + self.dist.rank)
@@ -296,7 +338,7 @@ class Rows(Workload):
         self.beta = (0.02 * rng.standard_normal(COLS)).astype(np.float32)
 
     def config(self):
-        return {"workload": "softmax_layernorm_rows_f32", "rows": ROWS, "cols": COLS, "seed": 0,
+        return {"workload": self.name, "rows": ROWS, "cols": COLS, "seed": 0,
                 "bytes_per_step": self.bytes_per_step,
                 "l2": "inputs larger than L2 (268 MB read per step), no flush"}
 
@@ -307,48 +349,46 @@ class Rows(Workload):
         self.db = torch.from_numpy(self.beta).cuda()
         self.out = torch.empty_like(self.dx)
         self.px = torch.from_numpy(self.x).pin_memory()
+        self.pg = torch.from_numpy(self.gamma).pin_memory()
+        self.pb = torch.from_numpy(self.beta).pin_memory()
         self.pout = torch.empty_like(self.px).pin_memory()
 
     def step_device(self):
         return self.module.device.softmax_layernorm(self.dx, self.dg, self.db, self.out).status
 
     def step_host(self):
-        return self.module.softmax_layernorm(self.px.view(-1), torch_from(self.gamma),
-                                             torch_from(self.beta), self.pout.view(-1)).status
+        return self.module.softmax_layernorm(self.px.view(-1), self.pg, self.pb,
+                                             self.pout.view(-1)).status
 
     def h2d_d2h(self):
         return 4 * ROWS * COLS + 8 * COLS, 4 * ROWS * COLS
 
-    def cpu_step(self, threads: int, oracle):
+    def cpu_step(self, threads: int, oracle) -> float:
         rows = 4096
-        oracle.softmax_layernorm(self.x[:rows], self.gamma, self.beta, threads=threads)
-        return 2 * 4 * rows * COLS
+        self.cpu_out = oracle.softmax_layernorm(self.x[:rows], self.gamma, self.beta,
+                                                threads=threads)
+        return 2.0 * 4 * rows * COLS
 
-    def check(self, oracle):
-        expected = oracle.softmax_layernorm(self.x[:256].copy(), self.gamma, self.beta)
-        got = self.out[:256].cpu().numpy()
-        return float(np.max(np.abs(got - expected) / np.maximum(np.abs(expected), 1.0)))
-
-
-def torch_from(array):
-    import torch
-
-    return torch.from_numpy(array)
+    def compare(self) -> float:
+        got = self.out[: self.cpu_out.shape[0]].cpu().numpy()
+        return float(np.max(np.abs(got - self.cpu_out) / np.maximum(np.abs(self.cpu_out), 1.0)))
 
 
 class Collatz(Workload):
+    name = "collatz_parallel_range"
     metric = "Collatz steps/s: parallel.range(1, 2^26) int64 sum and max of step counts"
     unit = "steps/s"
     dtype = "int64"
     kernel = "par_collatz_collatz_sum_0_part"
     scaling = "strong"
+    sample = "the starts [lo, lo + 2^22) of the range, repeated"
 
     def inputs(self):
         self.lo, self.hi = shard_range(1, COLLATZ_HI, self.dist.world, self.dist.rank)
-        self.total_steps = None
+        self.sum = None
 
     def config(self):
-        return {"workload": "collatz_parallel_range", "range": [1, COLLATZ_HI],
+        return {"workload": self.name, "range": [1, COLLATZ_HI],
                 "rank_range": [self.lo, self.hi], "l2": "no data: integer-issue bound"}
 
     def setup_device(self, runtime, torch):
@@ -361,25 +401,38 @@ class Collatz(Workload):
 
     step_host = step_device
 
+    def units(self) -> float:
+        return float(self.sum)
+
+    def job_units(self) -> float:
+        return float(self.dist.sum_i64([int(self.sum)])[0])
+
     def h2d_d2h(self):
         return 32, 16  # (lo, hi) twice in, (sum, max) out
 
-    def cpu_step(self, threads: int, oracle):
-        hi = min(self.hi, self.lo + (1 << 22))
-        status, total, _best = oracle.collatz(self.lo, hi, threads)
-        return total
+    def roofline(self, kernel_ms: float, peaks: dict) -> dict:
+        return {"bound": "int-issue", "achieved": self.units() / (kernel_ms / 1e3),
+                "peak": None, "unit": self.unit, "frac": None, "traffic": None,
+                "kernel": self.kernel, "kernel_ms": kernel_ms}
 
-    def check(self, oracle):
+    def cpu_step(self, threads: int, oracle) -> float:
+        hi = min(self.hi, self.lo + (1 << 22))
+        status, total, best = oracle.collatz(self.lo, hi, threads)
+        return float(total)
+
+    def compare(self) -> float:
         return 0.0
 
 
 class Gemm(Workload):
+    name = "matmul_bias_bf16"
     metric = "matmul TFLOP/s: C = A @ B + bias, bf16 A/B, f32 accumulate and C, 8192^3"
     unit = "TFLOP/s"
     dtype = "bf16"
     kernel = "matmul_bf16_pair_kernel"  # K = 8192: CTA pairs
     M = N = K = 8192
     flops = 2 * 8192 ** 3
+    sample = "NumPy f32 BLAS on the first 512 rows of A, repeated"
 
     def inputs(self):
         import torch
@@ -391,13 +444,15 @@ class Gemm(Workload):
         self.bias = 0.02 * torch.randn(self.N, generator=g)
 
     def config(self):
-        return {"workload": "matmul_bias_bf16", "m": self.M, "n": self.N, "k": self.K,
+        return {"workload": self.name, "m": self.M, "n": self.N, "k": self.K,
                 "seed": 0, "flops_per_step": self.flops,
                 "path": "tensor.matmul of tensor.convert(bf16) + bias through the built module: "
                         "B [K,N] transposed to K-major, then the tcgen05 kernel",
                 "l2": "operands 256 MB > L2, no flush"}
 
     def setup_device(self, runtime, torch):
+        import ctypes
+
         self.module = runtime.load(PREBUILT / "matmul_bf16_8192" / "matmul_bf16_8192.json")
         self.da, self.db, self.dbias = self.a.cuda(), self.b.cuda(), self.bias.cuda()
         self.out = torch.empty(self.M, self.N, device="cuda")
@@ -405,8 +460,6 @@ class Gemm(Workload):
         self.pbias = self.bias.pin_memory()
         self.pout = torch.empty(self.M, self.N).pin_memory()
         self.dbt = self.db.t().contiguous()
-        import ctypes
-
         self.lib = runtime.library()
         self.lib.ppyb200_matmul_bf16_kmajor.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
 
@@ -425,97 +478,155 @@ class Gemm(Workload):
                                                    self.dbias.data_ptr(), self.out.data_ptr(),
                                                    self.M, self.N, self.K)
 
+    def units(self) -> float:
+        return float(self.flops)
+
     def h2d_d2h(self):
         return 2 * 2 * self.M * self.K + 4 * self.N, 4 * self.M * self.N
 
-    def cpu_step(self, threads: int, oracle):
-        # NumPy f32 BLAS on the bf16-rounded values (the CPython reference of the path),
-        # over a bounded sample: the first 512 rows of A
+    def roofline(self, kernel_ms: float, peaks: dict) -> dict:
+        achieved = self.flops / (kernel_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "traffic": traffic(self.kernel),
+                "peak_source": f"{peaks['source']} cuBLAS bf16 (burst)", "kernel": self.kernel,
+                "kernel_ms": kernel_ms}
+
+    def cpu_step(self, threads: int, oracle) -> float:
+        # NumPy f32 BLAS on the bf16-rounded values (the CPython reference of the path)
         rows = 512
         a = self.a[:rows].float().numpy()
         b = self.b.float().numpy()
-        _ = a @ b + self.bias.numpy()
-        return 2 * rows * self.N * self.K
+        self.cpu_out = a @ b + self.bias.numpy()
+        return 2.0 * rows * self.N * self.K
 
-    def check(self, oracle):
-        import torch
-
-        rows = torch.tensor([0, 4095, 8191])
-        ref = self.a[rows].double() @ self.b.double() + self.bias.double()
-        got = self.out[rows.cuda()].cpu().double()
-        scale = torch.maximum(ref.abs(), ref.pow(2).mean().sqrt())
-        return float(((got - ref).abs() / scale).max())
+    def compare(self) -> float:
+        got = self.out[: self.cpu_out.shape[0]].cpu().numpy().astype(np.float64)
+        ref = self.cpu_out.astype(np.float64)
+        scale = np.maximum(np.abs(ref), np.sqrt(np.mean(ref ** 2)))
+        return float(np.max(np.abs(got - ref) / scale))
 
 
 class Gpt2(Workload):
-    metric = "GPT-2-124M forward tokens/s: batch 32 x 1024, logits out"
+    name = "gpt2_124m_forward"
+    metric = "GPT-2-124M forward tokens/s: batch 32 x 1024, f32 logits out"
     unit = "tokens/s"
     dtype = "bf16"
     kernel = "gpt2_forward"
     scaling = "strong"
     BATCH, LENGTH = 32, 1024
+    sample = ("torch CPU forward (f32, the reference's ATen ops) of the first sequence "
+              "(1 x 1024), repeated")
 
     def inputs(self):
         import torch
 
         start, stop = shard_batch(self.BATCH, self.dist.world, self.dist.rank)
         g = torch.Generator().manual_seed(0)
-        ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
+        ids = torch.randint(0, VOCAB, (self.BATCH, self.LENGTH), generator=g)
+        self.all_ids = ids
         self.ids = ids[start:stop].contiguous()
 
     def config(self):
-        return {"workload": "gpt2_124m_forward", "batch": self.BATCH, "seq_len": self.LENGTH,
-                "layers": 12, "width": 768, "heads": 12, "vocab": 50257,
-                "parallelism": f"dp{self.dist.world}", "weights": "N(0, 0.02) seed 0, bf16",
-                "l2": "weights 250 MB + activations > L2, no flush"}
+        b = self.ids.shape[0]
+        return {"workload": self.name, "batch": self.BATCH, "seq_len": self.LENGTH,
+                "layers": 12, "width": 768, "heads": 12, "vocab": VOCAB,
+                "parallelism": f"dp{self.dist.world}", "sequences_per_gpu": b,
+                "weights": "N(0, 0.02) seed 0, bf16; layernorm, softmax, residual and logits f32",
+                "launch": "eager" if self.eager else "one CUDA graph replay per forward",
+                "e2e_output": f"all logits: f32 [{b}, {self.LENGTH}, {VOCAB}] per GPU, copied "
+                              "into a contiguous pinned host array",
+                "l2": "weights 250 MB + activations and 6.6 GB of logits > L2, no flush"}
 
     def setup_device(self, runtime, torch):
         from ppy_b200 import gpt2
 
-        self.model = gpt2.GPT2(gpt2.GPT2_124M, seed=0)
         self.gpt2 = gpt2
-        self.dids = self.ids.cuda()
-        self.pids = self.ids.pin_memory()
+        self.model = gpt2.GPT2(gpt2.GPT2_124M, seed=0)
         b = self.ids.shape[0]
-        self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
-        self.last = torch.empty(b, 50257).pin_memory()
+        stream = torch.cuda.current_stream()
+        if self.eager:
+            self.dids = self.ids.cuda()
+            self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
+        else:
+            self.graphed = self.model.graphed(b, self.LENGTH, stream)
+            self.dids = self.graphed.ids
+            self.dids.copy_(self.ids)
+            self.logits = self.graphed.logits
+        self.pids = self.ids.pin_memory()
+        self.host_logits = torch.empty(b, self.LENGTH, VOCAB).pin_memory()
+        self.runtime = runtime
+
+    def _forward(self):
+        if self.eager:
+            self.model.forward(self.dids, self.logits)
+        else:
+            self.graphed.run()
 
     def step_device(self):
-        self.model.forward(self.dids, self.logits)
+        self._forward()
         return 0
 
     def step_host(self):
-        # e2e: ids from pinned host memory in, the last position's logits out (what the
-        # next-token step reads)
+        # e2e: the ids from pinned host memory in, every logit out into a contiguous host array
         self.dids.copy_(self.pids, non_blocking=True)
-        self.model.forward(self.dids, self.logits)
-        self.last.copy_(self.logits[:, -1], non_blocking=True)
+        self._forward()
+        self.runtime.copy_rows_to_host(self.host_logits, self.logits)
         return 0
+
+    def finish(self) -> int:
+        return self.model.status()
+
+    def units(self) -> float:
+        return float(self.ids.numel())
+
+    def job_units(self) -> float:
+        return float(self.dist.sum_i64([int(self.units())])[0])
 
     def h2d_d2h(self):
         b = self.ids.shape[0]
-        return 8 * b * self.LENGTH, 4 * b * 50257
+        return 8 * b * self.LENGTH, 4 * b * self.LENGTH * VOCAB
 
-    def cpu_step(self, threads: int, oracle):
-        # the reference's GPT-2 path is torch ATen: its CPU forward, one sequence of 1024,
-        # f32 weights (the bf16-rounded values)
+    def roofline(self, kernel_ms: float, peaks: dict) -> dict:
+        # per-kernel times from one eager forward with events around every call
+        table = self.model.profile(self.dids, self.logits)
+        name, (count, ms, flops) = max(table.items(), key=lambda kv: kv[1][1])
+        achieved = flops / (ms / 1e3) / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        forward_tflops = self.gpt2.sequence_flops(self.gpt2.GPT2_124M, self.ids.shape[0],
+                                                  self.LENGTH) / (kernel_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic(name),
+                "peak_source": f"{peaks['source']} cuBLAS bf16 (sustained)", "kernel": name,
+                "kernel_ms": ms / count, "forward_ms": kernel_ms,
+                "forward_tflops": forward_tflops, "forward_frac": forward_tflops / peak,
+                "breakdown_ms": {k: round(v[1], 3) for k, v in table.items()}}
+
+    def cpu_step(self, threads: int, oracle) -> float:
         import torch
+
+        from oracle import gpt2 as oracle_gpt2
 
         if not hasattr(self, "cpu_model"):
-            self.cpu_model = _cpu_reference_model()
+            self.cpu_model = oracle_gpt2.cpu_model(seed=0)
         torch.set_num_threads(threads)
         with torch.no_grad():
-            self.cpu_model(self.ids[:1])
+            self.cpu_out = self.cpu_model(self.all_ids[:1])
         return float(self.LENGTH)
 
-    def check(self, oracle):
-        import torch
+    def compare(self) -> float:
+        """Max error of sequence 0's logits against the CPU forward, per element against
+        max(|ref|, rms of ref): the 2e-2 bf16 tolerance's measure."""
+        got = self.logits[0].cpu().double()
+        ref = self.cpu_out[0].double()
+        scale = torch_max(ref.abs(), ref.pow(2).mean().sqrt())
+        return float(((got - ref).abs() / scale).max())
 
-        ids = self.dids[:1, :256]
-        got = self.model.forward(ids)
-        ref = self.model.reference_forward(ids)
-        torch.cuda.synchronize()
-        return float((got - ref).abs().max() / ref.abs().max())
+
+def torch_max(a, b):
+    import torch
+
+    return torch.maximum(a, b)
 
 
 class Gpt2TP(Gpt2):
@@ -524,10 +635,9 @@ class Gpt2TP(Gpt2):
     residual stream per block (T in {1, 2, 4}); N ranks form N/T such groups, each with its
     share of the batch (8 GPUs: 2 groups of 4). `--tp` picks T, 0 the widest that fits."""
 
-    metric = "GPT-2-124M forward tokens/s, tensor parallel: batch 32 x 1024, logits out"
+    name = "gpt2_124m_forward_tp"
+    metric = "GPT-2-124M forward tokens/s, tensor parallel: batch 32 x 1024, f32 logits out"
     kernel = "gpt2_tp_forward"
-    tp = 0
-    exchange = "nvlink"
 
     def inputs(self):
         import torch
@@ -537,7 +647,8 @@ class Gpt2TP(Gpt2):
         self.dp, self.tp = gpt2_tp.hybrid_layout(self.dist.world, gpt2.GPT2_124M, self.tp)
         start, stop = shard_batch(self.BATCH, self.dp, self.dist.rank // self.tp)
         g = torch.Generator().manual_seed(0)
-        ids = torch.randint(0, 50257, (self.BATCH, self.LENGTH), generator=g)
+        ids = torch.randint(0, VOCAB, (self.BATCH, self.LENGTH), generator=g)
+        self.all_ids = ids
         self.ids = ids[start:stop].contiguous()
 
     def config(self):
@@ -550,9 +661,11 @@ class Gpt2TP(Gpt2):
         else:
             exchange = (f"2 NCCL all-reduces (sum, f32 [{tokens}, 768]) per block inside "
                         f"each group of {self.tp}")
-        cfg.update(workload="gpt2_124m_forward_tp",
+        cfg.update(workload=self.name,
                    parallelism=f"tp{self.tp}" if self.dp == 1 else f"dp{self.dp}xtp{self.tp}",
-                   exchange=exchange)
+                   exchange=exchange, launch="eager",
+                   e2e_output="this rank's logits columns, copied into a contiguous pinned host "
+                              "array")
         return cfg
 
     def setup_device(self, runtime, torch):
@@ -564,77 +677,42 @@ class Gpt2TP(Gpt2):
         self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0, group=group,
                                                 exchange=self.exchange)
         self.gpt2 = gpt2
+        self.eager = True
         self.dids = self.ids.cuda()
         self.pids = self.ids.pin_memory()
         v0, v1 = self.model.shard.vocab
         b = self.ids.shape[0]
         self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
-        self.last = torch.empty(b, v1 - v0).pin_memory()
+        self.host_logits = torch.empty(b, self.LENGTH, v1 - v0).pin_memory()
+        self.runtime = runtime
+
+    def job_units(self) -> float:
+        return float(self.units()) * self.dp  # the ranks of a group share their tokens
 
     def h2d_d2h(self):
         v0, v1 = self.model.shard.vocab
         b = self.ids.shape[0]
-        return 8 * b * self.LENGTH, 4 * b * (v1 - v0)
+        return 8 * b * self.LENGTH, 4 * b * self.LENGTH * (v1 - v0)
 
-    def check(self, oracle):
-        import torch
+    def roofline(self, kernel_ms: float, peaks: dict) -> dict:
+        peak = peaks["bf16_tflops_sustained"]
+        per_gpu = self.gpt2.sequence_flops(self.gpt2.GPT2_124M, self.BATCH, self.LENGTH) / (
+            self.dist.world) / (kernel_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                "frac": per_gpu / peak, "traffic": None,
+                "peak_source": f"{peaks['source']} cuBLAS bf16 (sustained)",
+                "kernel": self.kernel, "kernel_ms": kernel_ms}
 
-        full = self.gpt2.GPT2(self.gpt2.GPT2_124M, seed=0)
-        ids = self.dids[:1, :256]
-        got = self.model.forward(ids)
+    def compare(self) -> float:
         v0, v1 = self.model.shard.vocab
-        ref = full.reference_forward(ids)[..., v0:v1]
-        torch.cuda.synchronize()
-        return float((got - ref).abs().max() / ref.abs().max())
+        got = self.logits[0].cpu().double()
+        ref = self.cpu_out[0, :, v0:v1].double()
+        scale = torch_max(ref.abs(), ref.pow(2).mean().sqrt())
+        return float(((got - ref).abs() / scale).max())
 
 
-def _cpu_reference_model():
-    """The GPT-2 forward of examples/46_gpt2/gpt2.ppy:18-57 (torch ATen ops) on the CPU, the
-    same shapes and init, f32."""
-    import torch
-    import torch.nn.functional as F
-
-    g = torch.Generator().manual_seed(0)
-    c, v, layers, heads = 768, 50257, 12, 12
-
-    def normal(*shape):
-        return (0.02 * torch.randn(*shape, generator=g)).to(torch.bfloat16).float()
-
-    wte, wpe = normal(v, c), normal(1024, c)
-    blocks = [(normal(3 * c, c), normal(c, c), normal(4 * c, c), normal(c, 4 * c))
-              for _ in range(layers)]
-    ones, zeros = torch.ones(c), torch.zeros(c)
-
-    def forward(ids):
-        b, n = ids.shape
-        x = wte[ids] + wpe[:n]
-        for wqkv, wo, wfc, wproj in blocks:
-            h = F.layer_norm(x, (c,), ones, zeros, 1e-5)
-            q, k, vv = F.linear(h, wqkv).split(c, dim=-1)
-            shape = lambda t: t.reshape(b, n, heads, c // heads).transpose(1, 2)  # noqa: E731
-            a = F.scaled_dot_product_attention(shape(q), shape(k), shape(vv), is_causal=True)
-            x = x + F.linear(a.transpose(1, 2).reshape(b, n, c), wo)
-            f = F.gelu(F.linear(F.layer_norm(x, (c,), ones, zeros, 1e-5), wfc), approximate="tanh")
-            x = x + F.linear(f, wproj)
-        return F.layer_norm(x, (c,), ones, zeros, 1e-5) @ wte.t()
-
-    return forward
-
-
-WORKLOADS = {"gelu": Gelu, "rows": Rows, "collatz": Collatz, "gemm": Gemm, "gpt2": Gpt2,
-             "gpt2_tp": Gpt2TP}
-
-
-def units_per_step(w: Workload) -> float:
-    if isinstance(w, Gemm):
-        return float(w.flops)
-    if isinstance(w, Gpt2):
-        return float(w.ids.numel())
-    if isinstance(w, Collatz):
-        if w.total_steps is None:
-            w.total_steps = w.sum
-        return float(w.total_steps)
-    return float(w.bytes_per_step)
+WORKLOADS = {"gpt2": Gpt2, "gpt2_tp": Gpt2TP, "gelu": Gelu, "rows": Rows, "collatz": Collatz,
+             "gemm": Gemm}
 
 
 def to_metric(w: Workload, units: float, seconds: float) -> float:
@@ -646,27 +724,26 @@ def to_metric(w: Workload, units: float, seconds: float) -> float:
 
 
 def cpu_baseline(w: Workload, seconds: float) -> dict:
+    """The oracle (or, for GPT-2, the reference's torch path) on the host cores over a
+    bounded sample, and the device output's error against it on that sample."""
     import oracle
 
     threads = oracle.threads_available()
     done = 0.0
-    start = time.perf_counter()
     steps = 0
+    start = time.perf_counter()
     while True:
         done += w.cpu_step(threads, oracle)
         steps += 1
         elapsed = time.perf_counter() - start
         if elapsed >= seconds:
             break
-    sample = {"gpt2": "torch CPU forward (f32) of the first sequence (1 x 1024), repeated",
-              "gpt2_tp": "torch CPU forward (f32) of the first sequence (1 x 1024), repeated",
-              "gemm": "NumPy f32 BLAS on the first 512 rows of A, repeated",
-              "gelu": "first 2^22 elements of the batch, repeated",
-              "rows": "first 4096 rows of the batch, repeated",
-              "collatz": "starts [lo, lo + 2^22) of the range, repeated"}[
-        next(k for k, v in WORKLOADS.items() if isinstance(w, v))]
     return {"value": to_metric(w, done, elapsed), "unit": w.unit, "cores": threads,
-            "kind": "port", "sample": f"{sample}; {steps} passes in {elapsed:.1f} s"}
+            "kind": "port", "sample": f"{w.sample}; {steps} passes in {elapsed:.1f} s",
+            "max_rel_error_vs_device": w.compare()}
+
+
+# ---------------------------------------------------------------- the reference arm
 
 
 def run_reference(args, dist: Dist) -> None:
@@ -674,32 +751,111 @@ def run_reference(args, dist: Dist) -> None:
     if dist.rank != 0:
         dist.stop()
         return
-    w = WORKLOADS[args.workload](dist)
-    w.dist.world = 1
-    w.inputs()
     import oracle
 
     threads = oracle.threads_available()
-    for _ in range(args.warmup):
-        w.cpu_step(threads, oracle)
-    units = 0.0
-    start = time.perf_counter()
-    for _ in range(args.steps):
-        units += w.cpu_step(threads, oracle)
-    elapsed = time.perf_counter() - start
-    value = to_metric(w, units, elapsed)
+
+    def time_cpu(name: str, steps: int, warmup: int) -> tuple[Workload, float, float]:
+        w = WORKLOADS[name](dist)
+        w.dist.world = 1
+        w.inputs()
+        for _ in range(warmup):
+            w.cpu_step(threads, oracle)
+        units = 0.0
+        start = time.perf_counter()
+        for _ in range(steps):
+            units += w.cpu_step(threads, oracle)
+        elapsed = time.perf_counter() - start
+        return w, to_metric(w, units, elapsed), elapsed
+
+    w, value, elapsed = time_cpu(args.workload, args.steps, args.warmup)
     line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed / max(args.steps, 1) * 1e3, "higher_is_better": True,
             "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
             "config": w.config(), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": w.unit, "cores": threads, "kind": "port",
-                             "sample": "one bounded sample of the batch per step (oracle C "
-                                       "restatement of the reference's CPU loops, OpenMP)"},
+                             "sample": f"one bounded sample per step: {w.sample}"},
             "e2e": {"value": value, "unit": w.unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    extras = _extras(args)
+    if extras:
+        line["workloads"] = {}
+        for name in extras:
+            x, xv, _ = time_cpu(name, 10, 1)
+            line["workloads"][x.name] = {"metric": x.metric, "value": xv, "unit": x.unit,
+                                         "impl": "reference", "cores": threads,
+                                         "kind": "port", "sample": x.sample}
     print(json.dumps(line), flush=True)
     dist.stop()
+
+
+# ---------------------------------------------------------------- the B200 arm
+
+
+def _extras(args) -> list[str]:
+    if args.workload != "gpt2" or args.extras in ("", "none"):
+        return []
+    return [x for x in args.extras.split(",") if x]
+
+
+def measure(w: Workload, steps: int, warmup: int, dist: Dist, stream, runtime, torch,
+            clocks: Clocks, peaks: dict) -> dict:
+    """Warm up, then time `steps` device-resident steps and `steps` host-memory steps, each
+    between one pair of CUDA events on `stream`, bracketed by a barrier and a synchronize;
+    the time is the max over ranks. Returns the workload's figures."""
+    for _ in range(max(warmup, 3)):
+        assert w.step_device() == 0
+        assert w.step_host() == 0
+    torch.cuda.synchronize()
+    launches0 = runtime.launches()
+
+    def timed(step) -> float:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        begin = time.perf_counter()
+        start.record(stream)
+        for _ in range(steps):
+            if step() != 0:
+                raise SystemExit(f"{w.name}: a step failed")
+        end.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        clocks.mark(begin, time.perf_counter())
+        return dist.max(start.elapsed_time(end))
+
+    device_ms = timed(w.step_device)
+    if getattr(w, "finish", None) is not None and w.finish() != 0:
+        raise SystemExit(f"{w.name}: a kernel raised its status word")
+    # the dominant kernel's own launch duration, for workloads whose step is more than it
+    kernel_ms = device_ms / steps
+    if hasattr(w, "kernel_step"):
+        k0 = torch.cuda.Event(enable_timing=True)
+        k1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        k0.record(stream)
+        for _ in range(steps):
+            if w.kernel_step() != 0:
+                raise SystemExit(f"{w.name}: the kernel step failed")
+        k1.record(stream)
+        torch.cuda.synchronize()
+        kernel_ms = k0.elapsed_time(k1) / steps
+    e2e_ms = timed(w.step_host)
+    launches = runtime.launches() - launches0
+    job = w.job_units()
+    h2d, d2h = w.h2d_d2h()
+    result = {"metric": w.metric, "value": to_metric(w, job * steps, device_ms / 1e3),
+              "unit": w.unit, "ms_per_step": device_ms / steps, "steps": steps,
+              "scaling": w.scaling, "dtype": w.dtype, "config": w.config(),
+              "e2e": {"value": to_metric(w, job * steps, e2e_ms / 1e3), "unit": w.unit,
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "ms_per_step": e2e_ms / steps},
+              "gpu_launches": int(launches)}
+    if dist.rank == 0:
+        result["roofline"] = w.roofline(kernel_ms, peaks)
+    return result
 
 
 def run_b200(args, dist: Dist) -> None:
@@ -710,143 +866,50 @@ def run_b200(args, dist: Dist) -> None:
     torch.cuda.set_device(dist.local)
     dist.start("nccl")
     runtime.init(dist.local)
-    # one stream for everything: the module's launches, copies and the timing events
+    # one stream for everything: the launches, copies, graph replays and the timing events
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     runtime.set_stream(stream)
-    w = WORKLOADS[args.workload](dist)
-    w.tp = args.tp
-    w.exchange = args.exchange
-    w.inputs()
-    w.setup_device(runtime, torch)
+    peaks = measured_peaks()
     clocks = Clocks(dist.local)
     clocks.start()
-    for _ in range(max(args.warmup, 3)):
-        assert w.step_device() == 0
-        assert w.step_host() == 0
-    torch.cuda.synchronize()
-    # device-resident timing: K steps back to back between one event pair
-    start_event = torch.cuda.Event(enable_timing=True)
-    end_event = torch.cuda.Event(enable_timing=True)
-    launches0 = runtime.launches()
-    dist.barrier()
-    torch.cuda.synchronize()
-    begin = time.perf_counter()
-    start_event.record(stream)
-    for _ in range(args.steps):
-        status = w.step_device()
-        if status != 0:
-            raise SystemExit(f"step failed with status {status}")
-    end_event.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    end = time.perf_counter()
-    clocks.mark(begin, end)
-    launches = runtime.launches() - launches0
-    total_ms = dist.max(start_event.elapsed_time(end_event))
-    # the dominant kernel's own launch duration (for the workloads whose step is more than
-    # that one launch, timed alone over the same number of launches)
-    if hasattr(w, "kernel_step"):
-        k0 = torch.cuda.Event(enable_timing=True)
-        k1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        k0.record(stream)
-        for _ in range(args.steps):
-            if w.kernel_step() != 0:
-                raise SystemExit("kernel step failed")
-        k1.record(stream)
-        torch.cuda.synchronize()
-        step_ms = [k0.elapsed_time(k1) / args.steps]
-    else:
-        step_ms = [total_ms / args.steps]
-    units = units_per_step(w)
-    units_all = units * (dist.world if w.scaling == "weak" else 1)
-    if isinstance(w, Collatz):
-        sums = dist.sum_i64([w.sum])
-        units_all = float(sums[0])
-    if isinstance(w, Gpt2TP):
-        units_all = float(units) * w.dp  # the ranks of a group share their tokens
-    elif isinstance(w, Gpt2):
-        units_all = float(dist.sum_i64([int(units)])[0])
-    value = to_metric(w, units_all * args.steps, total_ms / 1e3)
-    kernel_ms = float(np.mean(step_ms))
-    # end to end through the host-memory entry point (pinned host buffers)
-    e_start = torch.cuda.Event(enable_timing=True)
-    e_end = torch.cuda.Event(enable_timing=True)
-    dist.barrier()
-    torch.cuda.synchronize()
-    launches1 = runtime.launches()
-    e_start.record(stream)
-    for _ in range(args.steps):
-        if w.step_host() != 0:
-            raise SystemExit("host-memory step failed")
-    e_end.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    launches += runtime.launches() - launches1
-    e2e_ms = dist.max(e_start.elapsed_time(e_end))
-    e2e = to_metric(w, units_all * args.steps, e2e_ms / 1e3)
-    clock_info = clocks.stop()
-    import oracle
 
-    error = w.check(oracle)
+    def make(name: str) -> Workload:
+        w = WORKLOADS[name](dist)
+        w.tp, w.exchange, w.eager = args.tp, args.exchange, args.eager
+        w.inputs()
+        w.setup_device(runtime, torch)
+        return w
+
+    main = make(args.workload)
+    result = measure(main, args.steps, args.warmup, dist, stream, runtime, torch, clocks, peaks)
+    main_windows = list(clocks.windows)
+    extras = []
+    for name in _extras(args):
+        x = make(name)
+        extras.append((x, measure(x, max(args.steps, 100), args.warmup, dist, stream, runtime,
+                                  torch, clocks, peaks)))
+    clocks.stop()
     if dist.rank == 0:
-        pk = peaks()
-        h2d, d2h = w.h2d_d2h()
-        line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": dist.world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-                "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None,
-                "dtype": w.dtype, "data": "synthetic (seeded)", "config": w.config(),
-                "e2e": {"value": e2e, "unit": w.unit, "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h},
-                "gpu_launches": int(launches), "clocks": clock_info,
-                "max_rel_error_vs_oracle": error}
-        if w.unit == "TFLOP/s":
-            pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] if (
-                REPO / "MEASURED_PEAKS.json").exists() else 1590.0
-            achieved = w.flops / (kernel_ms / 1e3) / 1e12
-            line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk_t,
-                                "unit": "TFLOP/s", "frac": achieved / pk_t,
-                                "traffic": traffic(w.kernel), "peak_source": pk["source"],
-                                "kernel": w.kernel, "kernel_ms": kernel_ms}
-        elif w.unit == "GB/s":
-            achieved = w.bytes_per_step / (kernel_ms / 1e3) / 1e9
-            line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
-                                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                                "traffic": traffic(w.kernel), "peak_source": pk["source"],
-                                "kernel": w.kernel, "kernel_ms": kernel_ms}
-        elif isinstance(w, Gpt2TP):
-            pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (
-                REPO / "MEASURED_PEAKS.json").exists() else 1400.0
-            per_gpu = w.gpt2.sequence_flops(w.gpt2.GPT2_124M, w.BATCH, w.LENGTH) / dist.world / (
-                total_ms / args.steps / 1e3) / 1e12
-            line["roofline"] = {"bound": "tensor", "achieved": per_gpu, "peak": pk_t,
-                                "unit": "TFLOP/s", "frac": per_gpu / pk_t, "traffic": None,
-                                "peak_source": "measured (sustained)", "kernel": w.kernel,
-                                "kernel_ms": total_ms / args.steps}
-        elif isinstance(w, Gpt2):
-            pk_t = json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (
-                REPO / "MEASURED_PEAKS.json").exists() else 1400.0
-            table = w.model.profile(w.dids, w.logits)
-            name, (count, ms, flops) = max(table.items(), key=lambda kv: kv[1][1])
-            achieved = flops / (ms / 1e3) / 1e12
-            forward_tflops = w.gpt2.sequence_flops(w.gpt2.GPT2_124M, w.ids.shape[0],
-                                                   w.LENGTH) / (total_ms / args.steps / 1e3) / 1e12
-            line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk_t,
-                                "unit": "TFLOP/s", "frac": achieved / pk_t, "traffic": None,
-                                "peak_source": "measured (sustained)", "kernel": name,
-                                "kernel_ms": ms / count,
-                                "forward_tflops": forward_tflops,
-                                "forward_frac": forward_tflops / pk_t,
-                                "breakdown_ms": {k: round(v[1], 3) for k, v in table.items()}}
-        else:
-            line["roofline"] = {"bound": "int-issue", "achieved": value, "peak": None,
-                                "unit": w.unit, "frac": None, "traffic": None,
-                                "kernel": w.kernel, "kernel_ms": kernel_ms}
+        line = {"metric": main.metric, "value": result["value"], "unit": main.unit,
+                "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": result["ms_per_step"], "higher_is_better": True,
+                "scaling": main.scaling, "vs_baseline": None, "dtype": main.dtype,
+                "data": "synthetic (seeded)", "config": main.config(), "e2e": result["e2e"],
+                "gpu_launches": result["gpu_launches"] + sum(r["gpu_launches"] for _, r in extras),
+                "clocks": clocks.summary(main_windows), "roofline": result["roofline"]}
         if dist.world == 1:
-            line["cpu_baseline"] = cpu_baseline(w, args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(main, args.cpu_seconds)
+        if extras:
+            line["workloads"] = {}
+            for x, r in extras:
+                entry = dict(r)
+                if dist.world == 1:
+                    entry["cpu_baseline"] = cpu_baseline(x, args.cpu_seconds)
+                line["workloads"][x.name] = entry
+            line["workloads_clocks"] = clocks.summary(clocks.windows[len(main_windows):])
         print(json.dumps(line), flush=True)
-    close = getattr(getattr(w, "model", None), "close", None)
+    close = getattr(getattr(main, "model", None), "close", None)
     if close is not None:
         close()  # the tensor-parallel exchange buffers: every rank of the group together
     dist.stop()

@@ -54,7 +54,9 @@ int32_t ppyb200_device_count(void);
 
 /* Make `device` the calling thread's device (cudaSetDevice) and create its state.
  * Replaces ppy_runtime/cuda.py:51-57 (`Driver` binds device 0's primary context);
- * here every device of the node may be bound, one per calling thread. */
+ * here every device of the node may be bound, one per calling thread. It also loads the
+ * device code and static array of ppyb200_colmax_abs_f32_noalloc onto the device, so that
+ * no later call of that entry point allocates. */
 int32_t ppyb200_init(int32_t device);
 
 /* The calling thread's device, or -1 before ppyb200_init. */
@@ -99,12 +101,25 @@ void ppyb200_release_buffer(void *pointer);
 int32_t ppyb200_copy_to_device(void *device_dst, const void *host_src, int64_t bytes);
 int32_t ppyb200_copy_to_host(void *host_dst, const void *device_src, int64_t bytes);
 
+/* `rows` rows of `row_bytes` each from device memory (rows `device_pitch` bytes apart) into
+ * host memory (rows `host_pitch` bytes apart), one strided copy on the current stream (async):
+ * e.g. GPT-2's logits, computed into rows padded to 128-byte lines, into a contiguous host
+ * array. The reference's runtime copies whole contiguous arrays (ppy_runtime/cuda.py:125-126, `download`);
+ * this is the strided form of that copy-out. */
+int32_t ppyb200_copy_rows_to_host(void *host_dst, int64_t host_pitch, const void *device_src,
+                                  int64_t device_pitch, int64_t row_bytes, int64_t rows);
+
 /* Translate a cudaError_t into a status, recording `what` when it is a failure. */
 int32_t ppyb200_check(int32_t cuda_error, const char *what);
 
 /* Kernels launched through this library and the modules built against it. */
 uint64_t ppyb200_launches(void);
 void ppyb200_count_launches(uint64_t count);
+
+/* Device allocations (cudaMalloc) this runtime has made since the library loaded: scratch
+ * arenas, status words, cached buffers. No counterpart in the reference, whose runtime
+ * allocates per launch; it lets a caller check that a call allocated nothing. */
+uint64_t ppyb200_device_allocations(void);
 
 /* ---------------------------------------------------------------- matmul */
 
@@ -244,8 +259,12 @@ int32_t ppyb200_tp_accumulate(float *x, const float *bias, const float *exchange
  * reference: it exists for those callers. It allocates nothing -- its partial results live
  * in a static 1 MiB __device__ array (PPYB200_NOALLOC_PARTIALS floats) that every GPU
  * loading this library holds until exit -- and refuses rows wider than
- * PPYB200_NOALLOC_PARTIALS columns with PPYB200_RAISED. Its first call on a device looks
- * up the array's address (cudaGetSymbolAddress): make that call before any stream
+ * PPYB200_NOALLOC_PARTIALS columns with PPYB200_RAISED. CUDA loads device code lazily, and
+ * loading this entry point's module (the array with it) takes device memory: ppyb200_init
+ * does that for the device it binds, and looks up the array's address there
+ * (cudaGetSymbolAddress), so that after ppyb200_init no call allocates, through this
+ * library or the driver. Without ppyb200_init the first call on each device does the
+ * set-up: make that call before the caller reserves its memory and before any stream
  * capture. All calls share the array; calls that overlap on the GPU race on it. Device
  * pointers; enqueued on the current stream. */
 int32_t ppyb200_colmax_abs_f32_noalloc(const float *x, int64_t rows, int64_t cols, float *out);

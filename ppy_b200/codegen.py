@@ -852,12 +852,15 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
         lines.append(f"    if (!({' && '.join(align_checks)})) {{ ppyb200_set_error(\"{name}: "
                      f"row operands must be {vec * 4}-byte aligned\"); return PPY_STATUS_RAISED; }}")
     if pipelined:
-        lines += [f"    static int resident = 0;  // blocks of {name} one SM holds",
-                  "    if (resident == 0) {",
-                  f"      cudaFuncSetAttribute({name}, cudaFuncAttributeMaxDynamicSharedMemorySize, {smem_bytes});",
-                  f"      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, {name}, {block}, {smem_bytes});",
-                  "      if (resident < 1) resident = 1;",
-                  "    }",
+        lines += [f"    static ppyb200::DeviceOnce resident_on;  // blocks of {name} one SM holds",
+                  "    int resident = 0;",
+                  "    const cudaError_t set_up = resident_on.get([](int* v) {",
+                  f"      cudaError_t e = cudaFuncSetAttribute({name}, cudaFuncAttributeMaxDynamicSharedMemorySize, {smem_bytes});",
+                  f"      if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(v, {name}, {block}, {smem_bytes});",
+                  "      if (*v < 1) *v = 1;",
+                  "      return e;",
+                  "    }, &resident);",
+                  f"    if (set_up != cudaSuccess) return ppyb200_check((int32_t)set_up, \"{name}: set-up\");",
                   f"    const int64_t groups = (R + {rpw} - 1) / {rpw};",
                   f"    int64_t blocks = (groups + {warps} - 1) / {warps};",
                   "    const int64_t cap = (int64_t)ppyb200_sm_count() * resident;",

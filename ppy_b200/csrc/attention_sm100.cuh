@@ -559,13 +559,16 @@ inline cudaError_t launch(const __nv_bfloat16* qkv, const __nv_bfloat16* vt, __n
   if (!make_map(&map_qk, qkv, batch * length, 3 * width, 3 * width, BM) ||
       !make_map(&map_vt, vt, batch * heads * D, length, length, D))
     return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)shared_bytes());
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static gemm::DeviceOnce configured;
+  int ready = 0;
+  cudaError_t e = configured.get(
+      [](int* v) {
+        *v = 1;
+        return cudaFuncSetAttribute(causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)shared_bytes());
+      },
+      &ready);
+  if (e != cudaSuccess) return e;
   const int64_t items = batch * heads * ((length / BM + 1) / 2);
   const int grid = (int)(items < sm_count ? items : sm_count);
   const float scale_log2 = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)

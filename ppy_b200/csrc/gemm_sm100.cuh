@@ -783,21 +783,26 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---- host side
 
+using ppyb200::DeviceOnce;
+
 typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+inline EncodeTiled lookup_encode_tiled() {
+  void* entry = nullptr;
+  cudaDriverEntryPointQueryResult found;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &entry, cudaEnableDefault, &found) ==
+          cudaSuccess &&
+      found == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<EncodeTiled>(entry);
+  return nullptr;
+}
+
+// The driver's tensor-map encoder (the same function for every device), looked up once.
 inline EncodeTiled encode_tiled() {
-  static EncodeTiled fn = nullptr;
-  if (fn == nullptr) {
-    void* entry = nullptr;
-    cudaDriverEntryPointQueryResult found;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &entry, cudaEnableDefault, &found) ==
-            cudaSuccess &&
-        found == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(entry);
-  }
+  static const EncodeTiled fn = lookup_encode_tiled();
   return fn;
 }
 
@@ -833,14 +838,17 @@ inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt
   CUtensorMap map_a, map_b;
   if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN))
     return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(matmul_bf16_kernel<Epi>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)shared_bytes());
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static DeviceOnce configured;
+  int ready = 0;
+  cudaError_t e = configured.get(
+      [](int* v) {
+        *v = 1;
+        return cudaFuncSetAttribute(matmul_bf16_kernel<Epi>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)shared_bytes());
+      },
+      &ready);
+  if (e != cudaSuccess) return e;
   const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = (int)(tiles < sm_count ? tiles : sm_count);
   matmul_bf16_kernel<Epi><<<grid, THREADS, shared_bytes(), stream>>>(map_a, map_b, m, n, k, epi,
@@ -864,7 +872,7 @@ inline cudaError_t launch_pair(const __nv_bfloat16* a, const __nv_bfloat16* bt, 
   CUtensorMap map_a, map_b;
   if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN / 2))
     return cudaErrorInvalidValue;
-  static int max_clusters = 0;
+  static DeviceOnce resident;
   cudaLaunchConfig_t config = {};
   cudaLaunchAttribute attribute[1];
   attribute[0].id = cudaLaunchAttributeClusterDimension;
@@ -876,16 +884,21 @@ inline cudaError_t launch_pair(const __nv_bfloat16* a, const __nv_bfloat16* bt, 
   config.stream = stream;
   config.attrs = attribute;
   config.numAttrs = 1;
-  if (max_clusters == 0) {
-    cudaError_t e = cudaFuncSetAttribute(matmul_bf16_pair_kernel<Epi>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)pair_shared_bytes());
-    if (e != cudaSuccess) return e;
-    config.gridDim = dim3(2, 1, 1);
-    e = cudaOccupancyMaxActiveClusters(&max_clusters, matmul_bf16_pair_kernel<Epi>, &config);
-    if (e != cudaSuccess) return e;
-    if (max_clusters < 1) return cudaErrorInvalidConfiguration;
-  }
+  // the clusters of two CTAs that fit on this device at once (after the shared-memory
+  // attribute that lets the kernel launch at all)
+  int max_clusters = 0;
+  cudaError_t e = resident.get(
+      [&config](int* v) {
+        cudaError_t r = cudaFuncSetAttribute(matmul_bf16_pair_kernel<Epi>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)pair_shared_bytes());
+        if (r != cudaSuccess) return r;
+        cudaLaunchConfig_t probe = config;
+        probe.gridDim = dim3(2, 1, 1);
+        return cudaOccupancyMaxActiveClusters(v, matmul_bf16_pair_kernel<Epi>, &probe);
+      },
+      &max_clusters);
+  if (e != cudaSuccess) return e;
   const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
   const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
   config.gridDim = dim3((unsigned)(2 * clusters), 1, 1);

@@ -16,10 +16,15 @@
 // chunks is chosen so that chunks x cols fits, so any row count works, and a row wider
 // than PPYB200_NOALLOC_PARTIALS columns is refused before anything is launched.
 //
-// In host code the array's name is not a device address: the first call on each device
-// looks the address up with cudaGetSymbolAddress while that device is current, and every
-// later call on that device reuses it. That first call should therefore come before any
-// stream capture. All calls share the one array and it keeps the previous call's contents:
+// In host code the array's name is not a device address: it is looked up with
+// cudaGetSymbolAddress while the device is current, once per device, and reused. CUDA loads
+// a library's device code lazily, and the lookup is what loads this file's module -- the
+// array included -- onto the device, which takes device memory. So ppyb200_init does the
+// lookup (and loads both kernels) for the device it binds: after it, a call allocates
+// nothing at all, not even through the driver. A caller that never runs ppyb200_init gets
+// the lookup in its first call on each device instead; that call should then come before
+// any stream capture and before the caller reserves its device memory.
+// All calls share the one array and it keeps the previous call's contents:
 // each call writes every partial it later reads, so nothing has to start at zero, but calls
 // whose kernels overlap on the GPU (e.g. on two streams at once) race on it.
 #include <cuda_runtime.h>
@@ -41,20 +46,6 @@ static __device__ __align__(256) float g_colmax_partials[PPYB200_NOALLOC_PARTIAL
 std::mutex g_lock;
 float* g_partials[kMaxDevices] = {};
 
-// The device address of g_colmax_partials on the current device (looked up once).
-float* partials_address(int device) {
-  std::lock_guard<std::mutex> hold(g_lock);
-  if (g_partials[device] == nullptr) {
-    void* address = nullptr;
-    const cudaError_t error = cudaGetSymbolAddress(&address, g_colmax_partials);
-    if (error != cudaSuccess) {
-      ppyb200_check((int32_t)error, "ppyb200_colmax_abs_f32_noalloc: cudaGetSymbolAddress");
-      return nullptr;
-    }
-    g_partials[device] = static_cast<float*>(address);
-  }
-  return g_partials[device];
-}
 
 // Fold |x| over the rows of one chunk for one column; every (chunk, column) partial is
 // written, the identity (-inf) when the chunk holds no rows.
@@ -81,7 +72,45 @@ __global__ void __launch_bounds__(kThreads) colmax_final(const float* __restrict
   out[c] = acc;
 }
 
+// The device address of g_colmax_partials on the current device `device`, looked up once
+// per device; the first lookup also loads both kernels (cudaFuncGetAttributes), so that their
+// first launch loads nothing either.
+float* partials_address(int device) {
+  std::lock_guard<std::mutex> hold(g_lock);
+  if (g_partials[device] == nullptr) {
+    void* address = nullptr;
+    cudaError_t error = cudaGetSymbolAddress(&address, g_colmax_partials);
+    if (error != cudaSuccess) {
+      ppyb200_check((int32_t)error, "ppyb200_colmax_abs_f32_noalloc: cudaGetSymbolAddress");
+      return nullptr;
+    }
+    cudaFuncAttributes attributes;
+    error = cudaFuncGetAttributes(&attributes, colmax_partial);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, colmax_final);
+    if (error != cudaSuccess) {
+      ppyb200_check((int32_t)error, "ppyb200_colmax_abs_f32_noalloc: loading its kernels");
+      return nullptr;
+    }
+    g_partials[device] = static_cast<float*>(address);
+  }
+  return g_partials[device];
+}
+
 }  // namespace
+
+namespace ppyb200 {
+
+// Called by ppyb200_init with `device` current: load the module of this file on the device
+// and record the array's address there, so that no later call allocates.
+int32_t noalloc_prepare(int device) {
+  if (device < 0 || device >= kMaxDevices) {
+    ppyb200_set_error("ppyb200_colmax_abs_f32_noalloc: no such device");
+    return PPYB200_RAISED;
+  }
+  return partials_address(device) != nullptr ? PPYB200_OK : PPYB200_RAISED;
+}
+
+}  // namespace ppyb200
 
 extern "C" int32_t ppyb200_colmax_abs_f32_noalloc(const float* x, int64_t rows, int64_t cols,
                                                   float* out) {

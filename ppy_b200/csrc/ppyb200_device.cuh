@@ -19,6 +19,9 @@
 #include <stdint.h>
 #include <math.h>
 
+#include <atomic>
+#include <mutex>
+
 #define PPY_STATUS_OK 0
 #define PPY_STATUS_FALLBACK 1
 #define PPY_STATUS_RAISED (-1)
@@ -287,5 +290,39 @@ template <int PENDING>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(PENDING) : "memory");
 }
+
+// ---- host side
+
+// A value set up once per device for one kernel (its shared-memory attribute, its resident
+// cluster count): function attributes and occupancy belong to a device, and one process may
+// drive several devices from several threads. `get` runs `setup(int* value)` under a lock the
+// first time the calling thread's current device asks, keeps the positive value it gives, and
+// hands it back without the lock afterwards. A failed setup is retried by the next call.
+struct DeviceOnce {
+  static constexpr int kDevices = 64;
+  std::mutex lock;
+  std::atomic<int> value[kDevices];
+
+  template <class Setup>
+  cudaError_t get(Setup&& setup, int* out) {
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return e;
+    if (device < 0 || device >= kDevices) return cudaErrorInvalidDevice;
+    int v = value[device].load(std::memory_order_acquire);
+    if (v <= 0) {
+      std::lock_guard<std::mutex> hold(lock);
+      v = value[device].load(std::memory_order_relaxed);
+      if (v <= 0) {
+        e = setup(&v);
+        if (e != cudaSuccess) return e;
+        if (v <= 0) return cudaErrorInvalidConfiguration;
+        value[device].store(v, std::memory_order_release);
+      }
+    }
+    *out = v;
+    return cudaSuccess;
+  }
+};
 
 }  // namespace ppyb200

@@ -19,6 +19,10 @@
 
 #include "../../include/ppyb200.h"
 
+namespace ppyb200 {
+int32_t noalloc_prepare(int device);  // noalloc.cu
+}  // namespace ppyb200
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -42,6 +46,14 @@ struct DeviceState {
 std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
 std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_allocations{0};  // cudaMalloc calls that succeeded
+
+// cudaMalloc, counted (ppyb200_device_allocations).
+cudaError_t counted_malloc(void** pointer, size_t bytes) {
+  const cudaError_t error = cudaMalloc(pointer, bytes);
+  if (error == cudaSuccess) g_allocations.fetch_add(1);
+  return error;
+}
 
 thread_local int t_device = -1;
 thread_local cudaStream_t t_stream = nullptr;
@@ -112,9 +124,14 @@ int32_t ppyb200_init(int32_t device) {
   int32_t status = check(cudaSetDevice(device), "cudaSetDevice");
   if (status != PPYB200_OK) return status;
   t_device = device;
-  std::lock_guard<std::mutex> lock(g_mutex);
-  if (device_state_locked() == nullptr) return fail("ppyb200_init: could not create device state");
-  return PPYB200_OK;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (device_state_locked() == nullptr)
+      return fail("ppyb200_init: could not create device state");
+  }
+  // load the allocation-free reduction's module (its static array) now, while the caller
+  // can still afford device memory
+  return ppyb200::noalloc_prepare(device);
 }
 
 int32_t ppyb200_current_device(void) { return t_device; }
@@ -165,7 +182,7 @@ void* ppyb200_scratch(int64_t bytes) {
       ss->scratch_bytes = 0;
     }
     int64_t grown = size_class(bytes);
-    if (cudaMalloc(&ss->scratch, grown) != cudaSuccess) {
+    if (counted_malloc(&ss->scratch, grown) != cudaSuccess) {
       cudaGetLastError();
       fail("ppyb200_scratch: cudaMalloc failed");
       return nullptr;
@@ -185,7 +202,7 @@ int32_t* ppyb200_status_word(void) {
   cudaStream_t stream = current_stream_locked(state);
   StreamState* ss = stream_state_locked(state, stream);
   if (ss->status == nullptr) {
-    if (cudaMalloc(&ss->status, sizeof(int32_t)) != cudaSuccess ||
+    if (counted_malloc(reinterpret_cast<void**>(&ss->status), sizeof(int32_t)) != cudaSuccess ||
         cudaMallocHost(&ss->status_host, sizeof(int32_t)) != cudaSuccess) {
       cudaGetLastError();
       fail("ppyb200_status_word: allocation failed");
@@ -237,7 +254,7 @@ void* ppyb200_device_buffer(int64_t bytes) {
     return p;
   }
   void* p = nullptr;
-  if (cudaMalloc(&p, c) != cudaSuccess) {
+  if (counted_malloc(&p, c) != cudaSuccess) {
     cudaGetLastError();
     fail("ppyb200_device_buffer: cudaMalloc failed");
     return nullptr;
@@ -270,11 +287,24 @@ int32_t ppyb200_copy_to_host(void* host_dst, const void* device_src, int64_t byt
                "device-to-host copy");
 }
 
+int32_t ppyb200_copy_rows_to_host(void* host_dst, int64_t host_pitch, const void* device_src,
+                                  int64_t device_pitch, int64_t row_bytes, int64_t rows) {
+  if (rows <= 0 || row_bytes <= 0) return PPYB200_OK;
+  if (host_pitch < row_bytes || device_pitch < row_bytes)
+    return fail("ppyb200_copy_rows_to_host: pitches shorter than a row");
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(ppyb200_stream());
+  return check(cudaMemcpy2DAsync(host_dst, (size_t)host_pitch, device_src, (size_t)device_pitch,
+                                 (size_t)row_bytes, (size_t)rows, cudaMemcpyDeviceToHost, stream),
+               "device-to-host row copy");
+}
+
 int32_t ppyb200_check(int32_t cuda_error, const char* what) {
   return check(static_cast<cudaError_t>(cuda_error), what ? what : "CUDA call");
 }
 
 uint64_t ppyb200_launches(void) { return g_launches.load(); }
+
+uint64_t ppyb200_device_allocations(void) { return g_allocations.load(); }
 
 void ppyb200_count_launches(uint64_t count) { g_launches.fetch_add(count); }
 

@@ -88,11 +88,26 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// A 16-byte load of memory that peers store into while this kernel runs: relaxed at system
+// scope, never through the non-coherent (read-only) cache path that a const __restrict__
+// pointer would let the compiler choose. Ordered after the peers' stores by the waiting
+// thread's ld.acquire.sys of their flags and the __syncthreads that follows it.
+__device__ __forceinline__ float4 load_peer4(const float* p) {
+  float4 v;
+  asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
 // x[M,N] += bias[N] + sum_r exchange[r][M,N], after every flag reaches `epoch`. float4 per
 // thread (N % 4 == 0), grid-stride; one thread per block waits, the block follows it.
+// `exchange` is written by the peers up to the flags this kernel waits on, so it is read
+// with load_peer4, never as read-only data.
 __global__ void __launch_bounds__(256) tp_accumulate_kernel(
-    float* __restrict__ x, const float* __restrict__ bias, const float* __restrict__ exchange,
-    const int32_t* __restrict__ flags, int32_t ranks, int64_t m, int64_t n, int32_t epoch,
+    float* __restrict__ x, const float* __restrict__ bias, const float* exchange,
+    const int32_t* flags, int32_t ranks, int64_t m, int64_t n, int32_t epoch,
     int32_t* status) {
   __shared__ int ready;
   if (threadIdx.x == 0) {
@@ -120,7 +135,7 @@ __global__ void __launch_bounds__(256) tp_accumulate_kernel(
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 sum = b;
     for (int s = 0; s < ranks; ++s) {
-      const float4 p = *reinterpret_cast<const float4*>(exchange + s * slot + 4 * i);
+      const float4 p = load_peer4(exchange + s * slot + 4 * i);
       sum.x += p.x;
       sum.y += p.y;
       sum.z += p.z;

@@ -29,7 +29,7 @@ from pathlib import Path
 
 from . import runtime
 
-__all__ = ["Config", "GPT2", "GPT2_124M"]
+__all__ = ["Config", "GPT2", "GPT2_124M", "GraphedForward"]
 
 PREBUILT = Path(__file__).resolve().parent / "prebuilt"
 
@@ -278,33 +278,49 @@ class GPT2:
             return int(buffers["status"].item())
         return 0
 
-    # ---------------------------------------------------------------- the reference
+    def graphed(self, batch: int, length: int, stream) -> "GraphedForward":
+        """The forward over fixed device buffers of `batch` x `length` token ids, captured
+        once on `stream` into a CUDA graph (see GraphedForward)."""
+        return GraphedForward(self, batch, length, stream)
 
-    def reference_forward(self, ids):
-        """The same forward in float32 torch (the reference's ATen block of
-        examples/46_gpt2/gpt2.ppy:18-57 on these weights), for parity checks."""
+
+class GraphedForward:
+    """One GPT-2 forward captured into a CUDA graph: `ids` (int64 [batch, length]) in,
+    `logits` (f32 [batch, length, vocab], rows 128-byte aligned as new_logits) out, both
+    fixed device buffers. `run()` replays every kernel of the forward with one host call, so
+    the host's launch cost (about 90 C-ABI calls) drops out of the step: with few tokens per
+    GPU the kernels are short enough for it to matter. The graph is captured on `stream`
+    after one plain forward (which sets up the scratch buffers and each kernel's launch
+    attributes); replays go to `stream` too."""
+
+    def __init__(self, model: GPT2, batch: int, length: int, stream) -> None:
         import torch
-        import torch.nn.functional as F
 
-        cfg = self.config
-        batch, length = ids.shape
-        c, heads, hd = cfg.width, cfg.heads, cfg.head_dim
-        x = self.wte.float()[ids] + self.wpe.float()[:length]
-        for blk in self.blocks:
-            hh = F.layer_norm(x, (c,), blk["ln1_g"], blk["ln1_b"], 1e-5)
-            qkv = F.linear(hh, blk["w_qkv"].float(), blk["b_qkv"])
-            q, k, v = qkv.split(c, dim=-1)
-            q = q.reshape(batch, length, heads, hd).transpose(1, 2)
-            k = k.reshape(batch, length, heads, hd).transpose(1, 2)
-            v = v.reshape(batch, length, heads, hd).transpose(1, 2)
-            a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
-            a = a.transpose(1, 2).reshape(batch, length, c)
-            x = x + F.linear(a, blk["w_o"].float(), blk["b_o"])
-            n = F.layer_norm(x, (c,), blk["ln2_g"], blk["ln2_b"], 1e-5)
-            ff = F.gelu(F.linear(n, blk["w_fc"].float(), blk["b_fc"]), approximate="tanh")
-            x = x + F.linear(ff, blk["w_proj"].float(), blk["b_proj"])
-        n = F.layer_norm(x, (c,), self.lnf_g, self.lnf_b, 1e-5)
-        return n @ self.wte.float().t()
+        self.model = model
+        self.stream = stream
+        self.ids = torch.zeros(batch, length, dtype=torch.int64, device=model.device)
+        self.logits = model.new_logits(batch, length)
+        runtime.set_stream(stream)
+        with torch.cuda.stream(stream):
+            model.forward(self.ids, self.logits)
+        stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        before = runtime.launches()
+        with torch.cuda.graph(self.graph, stream=stream):
+            runtime.set_stream(stream)
+            model.forward(self.ids, self.logits)
+        runtime.set_stream(stream)
+        self.launches = runtime.launches() - before  # kernels one replay runs
+
+    def run(self):
+        """Replay the forward on the stream; counts its kernels as launched."""
+        self.graph.replay()
+        runtime.count_launches(self.launches)
+        return self.logits
+
+    def status(self) -> int:
+        """The device status word of the last replay (0 OK; 2 a kernel raised). Syncs."""
+        return self.model.status()
 
 
 def attention_flops(config: Config, batch: int, length: int) -> float:

@@ -13,6 +13,7 @@ backend's own passes first, as `ppy build <name>.ppy --backend b200` takes it. T
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -70,7 +71,9 @@ def from_source(path: Path):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, required=True)
+    parser.add_argument("--reference", type=Path, default=os.environ.get("PPY_REFERENCE"),
+                        required="PPY_REFERENCE" not in os.environ,
+                        help="a PPy checkout (default: $PPY_REFERENCE)")
     parser.add_argument("names", nargs="*", default=list(MODULES))
     options = parser.parse_args()
     sys.path.insert(0, str(options.reference / "src"))

@@ -66,6 +66,11 @@ def library() -> ctypes.CDLL:
         lib.ppyb200_set_stream.argtypes = [ctypes.c_void_p]
         lib.ppyb200_stream.restype = ctypes.c_void_p
         lib.ppyb200_launches.restype = ctypes.c_uint64
+        lib.ppyb200_device_allocations.restype = ctypes.c_uint64
+        lib.ppyb200_count_launches.argtypes = [ctypes.c_uint64]
+        lib.ppyb200_copy_rows_to_host.argtypes = [ctypes.c_void_p, ctypes.c_int64,
+                                                  ctypes.c_void_p, ctypes.c_int64,
+                                                  ctypes.c_int64, ctypes.c_int64]
         lib.ppyb200_scratch.restype = ctypes.c_void_p
         lib.ppyb200_scratch.argtypes = [ctypes.c_int64]
         lib.ppyb200_device_buffer.restype = ctypes.c_void_p
@@ -97,6 +102,37 @@ def set_stream(stream) -> None:
         return
     handle = int(getattr(stream, "cuda_stream", stream) or 0)
     library().ppyb200_set_stream(ctypes.c_void_p(handle or _LEGACY_STREAM))
+
+
+def device_allocations() -> int:
+    """cudaMalloc calls the runtime library has made since it loaded."""
+    return int(library().ppyb200_device_allocations())
+
+
+def count_launches(count: int) -> None:
+    """Add `count` kernels to the launch counter (launches a CUDA graph replays)."""
+    library().ppyb200_count_launches(ctypes.c_uint64(count))
+
+
+def copy_rows_to_host(host, device) -> None:
+    """Copy the rows of a 2-D (or batched) CUDA tensor `device` into the pinned host tensor
+    `host` of the same shape and dtype, both with unit stride along the last axis and evenly
+    spaced rows, with one strided copy on the current stream (asynchronous)."""
+    rows = device.numel() // device.shape[-1]
+    row_bytes = device.shape[-1] * device.element_size()
+    if tuple(host.shape) != tuple(device.shape) or host.dtype != device.dtype:
+        raise B200Error("copy_rows_to_host: the same shape and dtype on both sides")
+    pitches = []
+    for t in (host, device):
+        if t.stride(-1) != 1 or (t.dim() > 2 and t.stride(-3) != t.shape[-2] * t.stride(-2)):
+            raise B200Error("copy_rows_to_host: unit stride along rows, rows evenly spaced")
+        pitches.append(t.stride(-2) * t.element_size())
+    status = library().ppyb200_copy_rows_to_host(
+        ctypes.c_void_p(host.data_ptr()), ctypes.c_int64(pitches[0]),
+        ctypes.c_void_p(device.data_ptr()), ctypes.c_int64(pitches[1]),
+        ctypes.c_int64(row_bytes), ctypes.c_int64(rows))
+    if status != STATUS_OK:
+        raise B200Error(last_error())
 
 
 def launches() -> int:

@@ -2,11 +2,11 @@
 seeded inputs of the benchmark's shapes, so `ncu -k <kernel> -s <warm-up> -c 1` can capture
 one launch of it alone.
 
-    python -m ppy_b200.profile_cases gemm        # matmul_bf16_pair_kernel, 8192^3, K-major B
-    python -m ppy_b200.profile_cases attention   # causal_kernel, batch 32 x 1024, 12 heads
-    python -m ppy_b200.profile_cases fc          # matmul_bf16_pair_kernel, GELU epilogue,
+    python profile_cases.py gemm        # matmul_bf16_pair_kernel, 8192^3, K-major B
+    python profile_cases.py attention   # causal_kernel, batch 32 x 1024, 12 heads
+    python profile_cases.py fc          # matmul_bf16_pair_kernel, GELU epilogue,
                                                  # GPT-2 FC (32768 x 3072 x 768)
-    python -m ppy_b200.profile_cases lm_head     # matmul_bf16_pair_kernel, quads epilogue,
+    python profile_cases.py lm_head     # matmul_bf16_pair_kernel, quads epilogue,
                                                  # 50257 logits a row in rows 50272 apart
 
 Each case launches its kernel three times (two warm-ups, then the one to capture: `-s 2`).
@@ -17,12 +17,16 @@ per tile for a capture of `matmul_bf16_kernel`.
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent))
 
 
 def main() -> None:
     import torch
 
-    from . import gpt2, runtime
+    from ppy_b200 import gpt2, runtime
 
     parser = argparse.ArgumentParser()
     parser.add_argument("case", choices=["gemm", "attention", "fc", "lm_head"])

@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -10,7 +11,10 @@ import pytest
 REPO = Path(__file__).resolve().parents[1]
 GOLDEN = REPO / "tests" / "golden"
 PREBUILT = REPO / "ppy_b200" / "prebuilt"
-REFERENCE = Path("/root/reference")
+# A checkout of the PPy reference (its `src/` holds `ppy_compiler`): the directory the
+# PPY_REFERENCE environment variable names, else a checkout called `reference` beside this
+# repository. Tests that run PPy's own compiler skip without one; no GPU test needs it.
+REFERENCE = Path(os.environ.get("PPY_REFERENCE", str(REPO.parent / "reference")))
 
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))

@@ -15,7 +15,7 @@ writes:
 * ``collatz.json`` -- ``ppy run`` output of the Collatz program (LLVM backend,
   ``threads``) and the JIT status of an overflowing range.
 
-Run:  python tests/golden/make_golden.py --reference /root/reference
+Run:  python tests/golden/make_golden.py --reference <a PPy checkout>  (or set PPY_REFERENCE)
 """
 
 from __future__ import annotations
@@ -756,7 +756,9 @@ def golden_collatz(reference: Path) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, required=True)
+    parser.add_argument("--reference", type=Path, default=os.environ.get("PPY_REFERENCE"),
+                        required="PPY_REFERENCE" not in os.environ,
+                        help="a PPy checkout (default: $PPY_REFERENCE)")
     parser.add_argument("--only", help="write one fixture (e.g. views) and no other")
     options = parser.parse_args()
     _setup(options.reference)

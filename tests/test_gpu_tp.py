@@ -34,6 +34,7 @@ def _rank(rank: int, world: int, port: int, queue, tp: int = 0, exchange: str = 
     import torch.distributed as dist
 
     sys.path.insert(0, str(REPO))
+    from oracle import gpt2 as oracle_gpt2
     from ppy_b200 import gpt2, gpt2_tp, runtime
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -59,7 +60,7 @@ def _rank(rank: int, world: int, port: int, queue, tp: int = 0, exchange: str = 
         full = gpt2.GPT2(cfg, seed=0)
         v0, v1 = tp.shard.vocab
         one_gpu = full.forward(ids)[..., v0:v1]
-        ref = full.reference_forward(ids)[..., v0:v1]
+        ref = oracle_gpt2.forward(full, ids)[..., v0:v1]
         torch.cuda.synchronize()
         diff = (got - ref).double()
         queue.put((rank, status, float(diff.abs().max() / ref.abs().max()),

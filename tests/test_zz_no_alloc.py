@@ -62,6 +62,30 @@ def test_no_alloc_colmax_matches_the_allocating_entry_point_twice(lib):
         assert torch.isnan(out[5]) and torch.isnan(expected[5])
 
 
+def test_no_alloc_colmax_allocates_nothing_once_the_device_is_bound(lib):
+    """The property the entry point exists for. ppyb200_init (in the fixture) loads its code
+    and static array onto the device; from then on calls on shapes it has not seen allocate
+    nothing: neither this library's cudaMalloc count nor the device's free memory moves."""
+    from ppy_b200 import runtime
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    shapes = [(123_457, 17), (3, 262_144), (4096, 1000)]
+    inputs = [torch.randn(rows, cols, device="cuda", generator=g) for rows, cols in shapes]
+    outs = [torch.empty(cols, device="cuda") for _, cols in shapes]
+    warm = torch.randn(512, 64, device="cuda", generator=g)
+    warm_out = torch.empty(64, device="cuda")
+    assert lib.ppyb200_colmax_abs_f32_noalloc(warm.data_ptr(), 512, 64, warm_out.data_ptr()) == 0
+    torch.cuda.synchronize()
+    before = (runtime.device_allocations(), torch.cuda.mem_get_info()[0])
+    for x, out, (rows, cols) in zip(inputs, outs, shapes):
+        assert lib.ppyb200_colmax_abs_f32_noalloc(x.data_ptr(), rows, cols, out.data_ptr()) == 0
+    torch.cuda.synchronize()
+    after = (runtime.device_allocations(), torch.cuda.mem_get_info()[0])
+    assert after == before
+    for x, out in zip(inputs, outs):
+        assert torch.equal(out, x.abs().amax(dim=0))
+
+
 def test_no_alloc_colmax_refuses_rows_wider_than_its_array(lib):
     from ppy_b200 import runtime
 
