@@ -507,6 +507,83 @@ class Gemm(Workload):
         return float(np.max(np.abs(got - ref) / scale))
 
 
+class GemmF32(Gemm):
+    """The fp32-input variant: C = A @ B + bias with f32 A, B, bias and C at 4096^3, through
+    the module the backend builds from tests/golden/matmul_f32_4096.ppyir: a split pass
+    (A, B into tf32 high and low parts) and the tcgen05 GEMM over the three products."""
+
+    name = "matmul_bias_f32"
+    metric = "matmul TFLOP/s: C = A @ B + bias, f32 A/B/bias/C, 4096^3"
+    dtype = "f32"
+    kernel = "matmul_tf32x3_pair_kernel"
+    M = N = K = 4096
+    flops = 2 * 4096 ** 3
+    sample = "NumPy f32 BLAS on the first 512 rows of A, repeated"
+
+    def inputs(self):
+        import torch
+
+        g = torch.Generator().manual_seed(0 + self.dist.rank)
+        k = self.K
+        self.a = torch.randn(self.M, k, generator=g) / k ** 0.5
+        self.b = torch.randn(k, self.N, generator=g) / k ** 0.5
+        self.bias = 0.02 * torch.randn(self.N, generator=g)
+
+    def config(self):
+        return {"workload": self.name, "m": self.M, "n": self.N, "k": self.K, "seed": 0,
+                "flops_per_step": self.flops,
+                "path": "tensor.matmul of f32 operands + bias through the built module: A and B "
+                        "split into tf32 high and low parts, then one tcgen05 GEMM over "
+                        "A_hi.B_hi + A_hi.B_lo + A_lo.B_hi (K' = 3 K)",
+                "l2": "operands 128 MB + split operands 256 MB > L2, no flush"}
+
+    def setup_device(self, runtime, torch):
+        self.module = runtime.load(PREBUILT / "matmul_f32_4096" / "matmul_f32_4096.json")
+        self.da, self.db, self.dbias = self.a.cuda(), self.b.cuda(), self.bias.cuda()
+        self.out = torch.empty(self.M, self.N, device="cuda")
+        self.pa, self.pb = self.a.pin_memory(), self.b.pin_memory()
+        self.pbias = self.bias.pin_memory()
+        self.pout = torch.empty(self.M, self.N).pin_memory()
+        self.torch = torch
+
+    kernel_step = None  # the step (split + GEMM + the non-finite check) is the timed launch
+
+    def step_device(self):
+        return self.module.device.matmul_bias(self.da, self.db, self.dbias, self.out).status
+
+    def step_host(self):
+        return self.module.matmul_bias(self.pa, self.pb, self.pbias, self.pout).status
+
+    def h2d_d2h(self):
+        return 2 * 4 * self.M * self.K + 4 * self.N, 4 * self.M * self.N
+
+    def roofline(self, kernel_ms: float, peaks: dict) -> dict:
+        # the method's ceiling: three tf32 products at the device's tf32 rate, measured here
+        # with cuBLAS (torch.matmul with TF32 allowed, 8192^3, best of 5)
+        torch = self.torch
+        torch.backends.cuda.matmul.allow_tf32 = True
+        x = torch.randn(8192, 8192, device="cuda")
+        y = torch.randn(8192, 8192, device="cuda")
+        best = float("inf")
+        for _ in range(6):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(x, y)
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e))
+        torch.backends.cuda.matmul.allow_tf32 = False
+        tf32 = 2 * 8192 ** 3 / (best / 1e3) / 1e12
+        achieved = self.flops / (kernel_ms / 1e3) / 1e12
+        peak = tf32 / 3
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic(self.kernel),
+                "peak_source": f"cuBLAS tf32 measured in this run ({tf32:.0f} TFLOP/s) / 3 "
+                               "products",
+                "kernel": "split + " + self.kernel, "kernel_ms": kernel_ms,
+                "cublas_tf32_tflops": tf32}
+
+
 class Gpt2(Workload):
     name = "gpt2_124m_forward"
     metric = "GPT-2-124M forward tokens/s: batch 32 x 1024, f32 logits out"
@@ -712,7 +789,7 @@ class Gpt2TP(Gpt2):
 
 
 WORKLOADS = {"gpt2": Gpt2, "gpt2_tp": Gpt2TP, "gelu": Gelu, "rows": Rows, "collatz": Collatz,
-             "gemm": Gemm}
+             "gemm": Gemm, "gemm_f32": GemmF32}
 
 
 def to_metric(w: Workload, units: float, seconds: float) -> float:
@@ -831,7 +908,7 @@ def measure(w: Workload, steps: int, warmup: int, dist: Dist, stream, runtime, t
         raise SystemExit(f"{w.name}: a kernel raised its status word")
     # the dominant kernel's own launch duration, for workloads whose step is more than it
     kernel_ms = device_ms / steps
-    if hasattr(w, "kernel_step"):
+    if getattr(w, "kernel_step", None) is not None:
         k0 = torch.cuda.Event(enable_timing=True)
         k1 = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()

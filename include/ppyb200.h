@@ -121,6 +121,16 @@ void ppyb200_count_launches(uint64_t count);
  * allocates per launch; it lets a caller check that a call allocated nothing. */
 uint64_t ppyb200_device_allocations(void);
 
+/* Programmatic dependent launch: while on (the default), the tensor-core GEMMs, the
+ * attention kernel, the GPT-2 embedding and the row-group kernels are launched so that
+ * their CTAs may start, and set up, while the kernel before them on the stream drains;
+ * each waits (griddepcontrol.wait) for that kernel's results before it touches memory.
+ * Results are the same either way. No counterpart in the reference, which launches one
+ * kernel per call and waits for it. Process-wide; ppyb200_set_pdl returns the previous
+ * setting. */
+int32_t ppyb200_set_pdl(int32_t enabled);
+int32_t ppyb200_pdl(void);
+
 /* ---------------------------------------------------------------- matmul */
 
 /* C[M,N] = A[M,K] @ B[K,N] (+ bias[N]): bf16 A and B, row-major; f32 bias (NULL for none);
@@ -146,6 +156,19 @@ int32_t ppyb200_matmul_bf16_kmajor(const uint16_t *a, const uint16_t *bt, const 
  * row, go into rows 50272 apart. PPYB200_RAISED for ldc < N. */
 int32_t ppyb200_matmul_bf16_kmajor_ld(const uint16_t *a, const uint16_t *bt, const float *bias,
                                       float *c, int64_t ldc, int64_t m, int64_t n, int64_t k);
+
+/* C[M,N] = A[M,K] @ B[K,N] (+ bias[N]) for f32 A, B, bias (NULL for none) and C, row-major:
+ * LowerTensor.op_matmul (ir/transforms/lower_tensor.py:756-776) for f32 `tensor.matmul` /
+ * `linalg.matmul`, with the bias row FuseTensor leaves after it. On tcgen05 tensor cores as
+ * three tf32 products, A_hi B_hi + A_hi B_lo + A_lo B_hi, with x_hi = x rounded to tf32 and
+ * x_lo = (x - x_hi) rounded to tf32 (the split operands, 16 (M + N) Kp bytes with Kp = K
+ * rounded up to 32, go to the scratch arena): each product term is within about 2^-21 of
+ * |a||b| of the f32 product, the sum accumulated in f32. Inputs that are not finite are
+ * detected by the split, and C is then recomputed with f32 FMAs in k order (IEEE infinities
+ * and NaNs, as the reference's loop). Any M, N, K (K = 0 gives the bias); no alignment
+ * needed. Device pointers; enqueued on the current stream (four launches). */
+int32_t ppyb200_matmul_f32(const float *a, const float *b, const float *bias, float *c,
+                           int64_t m, int64_t n, int64_t k);
 
 /* bt[n*K + k] = b[k*N + n]: a bf16 [K,N] matrix into [N,K] (tiled through shared memory). */
 int32_t ppyb200_transpose_bf16(const uint16_t *b, uint16_t *bt, int64_t k, int64_t n);

@@ -619,6 +619,10 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
     L.append(f"  constexpr int VEC = {vec}, TPR = {tpr}, NCH = {nch}, CHUNKS = {chunks}, "
              f"COLS = {kernel.cols};")
     L.append("  (void)CHUNKS; (void)status;")
+    # launched with the programmatic-serialization attribute (ppyb200::launch_pdl): wait
+    # for the previous kernel's results, and let the next kernel's CTAs start setting up
+    L.append("  ppyb200::pdl_wait();")
+    L.append("  ppyb200::pdl_trigger();")
     if tpr <= 32:
         L.append("  const int lane = threadIdx.x % TPR;")
         L.append(f"  const int64_t slot = (threadIdx.x & 31) / TPR; constexpr int64_t RPW = 32 / TPR;")
@@ -865,12 +869,14 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
                   f"    int64_t blocks = (groups + {warps} - 1) / {warps};",
                   "    const int64_t cap = (int64_t)ppyb200_sm_count() * resident;",
                   "    if (blocks > cap) blocks = cap;",
-                  f"    {name}<<<(unsigned)blocks, {block}, {smem_bytes}, stream>>>({call_args});",
+                  f"    const cudaError_t launched = ppyb200::launch_pdl({name}, dim3((unsigned)blocks), dim3({block}), {smem_bytes}, stream, {call_args});",
+                  f"    if (launched != cudaSuccess) return ppyb200_check((int32_t)launched, \"{name}\");",
                   "    launches++;", "  }", "}"]
     else:
         rpb = layout["rows_per_block"]
         lines += [f"    const int64_t blocks = (R + {rpb} - 1) / {rpb};",
-                  f"    {name}<<<(unsigned)blocks, {block}, 0, stream>>>({call_args});",
+                  f"    const cudaError_t launched = ppyb200::launch_pdl({name}, dim3((unsigned)blocks), dim3({block}), 0, stream, {call_args});",
+                  f"    if (launched != cudaSuccess) return ppyb200_check((int32_t)launched, \"{name}\");",
                   "    launches++;", "  }", "}"]
     return {"launch": lines, "status": needs_status(kernel.program)}
 
@@ -1421,7 +1427,7 @@ def module_source(plan: P.ModulePlan, device_sources: list[str], kernels: list) 
         _scalar_function(fn, src)
     parts = [PRELUDE.replace("{module}", plan.name)]
     if any(k.kind == "matmul" for fn in plan.functions if fn.kind == "tensor" for k in fn.kernels):
-        parts.append('#include "gemm_sm100.cuh"\n#include "gemm_simt.cuh"')
+        parts.append('#include "gemm_sm100.cuh"\n#include "gemm_simt.cuh"\n#include "gemm_f32.cuh"')
     parts += prototypes
     parts += device_sources
     parts += src.kernels

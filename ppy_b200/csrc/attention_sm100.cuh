@@ -269,6 +269,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // the set-up above overlaps the previous kernel; its results are needed from here on
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == LOADER_WARP) {
     if (lane == 0) {
@@ -572,9 +575,8 @@ inline cudaError_t launch(const __nv_bfloat16* qkv, const __nv_bfloat16* vt, __n
   const int64_t items = batch * heads * ((length / BM + 1) / 2);
   const int grid = (int)(items < sm_count ? items : sm_count);
   const float scale_log2 = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
-  causal_kernel<<<grid, THREADS, shared_bytes(), stream>>>(map_qk, map_vt, out, batch, length,
-                                                           heads, scale_log2, status);
-  return cudaGetLastError();
+  return launch_pdl(causal_kernel, dim3(grid), dim3(THREADS), shared_bytes(), stream, map_qk,
+                    map_vt, out, batch, length, heads, scale_log2, status);
 }
 
 }  // namespace attention

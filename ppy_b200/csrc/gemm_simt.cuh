@@ -20,11 +20,15 @@ __device__ __forceinline__ float to_f32(T v) {
   return ppyb200::convert<float, T>(v);
 }
 
-// A 32x32 output tile per 32x8 block; every thread computes 4 outputs of one column.
+// A 32x32 output tile per 32x8 block; every thread computes 4 outputs of one column. With
+// `only_if` given, the kernel does nothing unless *only_if is nonzero (a recomputation that
+// an earlier kernel on the stream asks for).
 template <class T, class Epi>
 __global__ void __launch_bounds__(256) matmul_kernel(const T* __restrict__ a,
                                                      const T* __restrict__ b, int64_t m,
-                                                     int64_t n, int64_t k, Epi epi) {
+                                                     int64_t n, int64_t k, Epi epi,
+                                                     const int32_t* only_if) {
+  if (only_if != nullptr && *(volatile const int32_t*)only_if == 0) return;
   __shared__ float as[TILE][TILE + 1];
   __shared__ float bs[TILE][TILE + 1];
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -57,10 +61,10 @@ __global__ void __launch_bounds__(256) matmul_kernel(const T* __restrict__ a,
 
 template <class T, class Epi>
 inline cudaError_t launch(const T* a, const T* b, int64_t m, int64_t n, int64_t k, Epi epi,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const int32_t* only_if = nullptr) {
   if (m <= 0 || n <= 0) return cudaSuccess;
   dim3 grid((unsigned)((n + TILE - 1) / TILE), (unsigned)((m + TILE - 1) / TILE));
-  matmul_kernel<T, Epi><<<grid, dim3(32, 8), 0, stream>>>(a, b, m, n, k, epi);
+  matmul_kernel<T, Epi><<<grid, dim3(32, 8), 0, stream>>>(a, b, m, n, k, epi, only_if);
   return cudaGetLastError();
 }
 

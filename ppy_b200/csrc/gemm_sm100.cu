@@ -1,12 +1,13 @@
 // The C-ABI matmul entry points of libppyb200 (include/ppyb200.h): bf16 x bf16 -> f32 with
 // an optional f32 bias row, on tcgen05 tensor cores for whole 128x256x64 tiles and on the
-// CUDA cores otherwise.
+// CUDA cores otherwise; f32 x f32 -> f32 as three tf32 products on the tensor cores.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
 #include "../../include/ppyb200.h"
 #include "gemm_sm100.cuh"
+#include "gemm_f32.cuh"
 #include "gemm_simt.cuh"
 
 namespace {
@@ -83,6 +84,31 @@ int32_t ppyb200_matmul_bf16_kmajor_ld(const uint16_t* a, const uint16_t* bt, con
 int32_t ppyb200_matmul_bf16_kmajor(const uint16_t* a, const uint16_t* bt, const float* bias,
                                    float* c, int64_t m, int64_t n, int64_t k) {
   return ppyb200_matmul_bf16_kmajor_ld(a, bt, bias, c, n, m, n, k);
+}
+
+int32_t ppyb200_matmul_f32(const float* a, const float* b, const float* bias, float* c,
+                           int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k < 0) {
+    ppyb200_set_error("ppyb200_matmul_f32: negative extent");
+    return PPYB200_RAISED;
+  }
+  if (m == 0 || n == 0) return PPYB200_OK;
+  const int64_t kp = ppyb200::gemm::tf32_depth(k);
+  if (m >= (1ll << 31) || n >= (1ll << 31) || 2 * kp >= (1ll << 31)) {
+    ppyb200_set_error("ppyb200_matmul_f32: an extent beyond the tensor maps' int32 range");
+    return PPYB200_RAISED;
+  }
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(ppyb200_stream());
+  int32_t* status = ppyb200_status_word();
+  if (status == nullptr) return PPYB200_RAISED;
+  float* work = static_cast<float*>(ppyb200_scratch(ppyb200::gemm::tf32x3_work_bytes(m, n, k)));
+  if (work == nullptr) return PPYB200_RAISED;
+  // (K = 0 splits into one K-step of zeros: C = bias, the empty sum, as the reference's
+  // loop nest gives)
+  cudaError_t e = ppyb200::gemm::launch_tf32x3(a, b, work, m, n, k,
+                                               ppyb200::gemm::BiasEpilogue{bias, c, n}, status,
+                                               ppyb200_sm_count(), stream);
+  return finish(e, "ppyb200_matmul_f32", 4);
 }
 
 int32_t ppyb200_matmul_bf16(const uint16_t* a, const uint16_t* b, const float* bias, float* c,

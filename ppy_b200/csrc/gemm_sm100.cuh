@@ -60,6 +60,59 @@ constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                            ((uint32_t)(BM >> 4) << 24);
 
+// What a kernel's operands are. Every K-step loads one 128-byte swizzle row of each operand
+// row (64 bf16 or 32 f32) and issues four MMAs of 32 bytes of K each (K = 16 bf16, or K = 8
+// tf32), so the shared-memory layouts, descriptors and the ring are the same for both; what
+// differs is the element type of the TMA maps, the MMA kind, and which columns of the operand
+// matrices a K-step reads.
+//
+// Bf16Operands: A [M, K] and Bt [N, K], bf16; K-step kb reads columns kb*64 .. +63 of both.
+struct Bf16Operands {
+  using T = __nv_bfloat16;
+  static constexpr int kStep = 64;
+  static constexpr int kSegments = 1;
+  static constexpr uint32_t kFormat = 1;  // bf16 (kind::f16)
+  static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t) {
+    return (int32_t)(kb * kStep);
+  }
+  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t) {
+    return (int32_t)(kb * kStep);
+  }
+};
+
+// Tf32x3Operands: an f32 product A.B computed as three tf32 products on the tensor cores,
+// A_hi.B_hi + A_hi.B_lo + A_lo.B_hi, where x_hi is x rounded to tf32 (11 significant bits)
+// and x_lo is (x - x_hi) rounded to tf32: what is dropped is A_lo.B_lo and the third
+// 11-bit piece of each operand, both about 2^-22 of |a||b| (fp32 keeps 24 bits). The
+// operands are A2 [M, 2 Kp] = [A_hi | A_lo] and B2t [N, 2 Kp] = [B_hi^T | B_lo^T] (Kp = K
+// rounded up to 32, zero-filled), written by split_tf32 below; the kernel's K-steps walk
+// the three products back to back as one tf32 product of depth 3 Kp: for step kb of
+// segment s = kb / (Kp/32), A reads its hi half for s = 0, 1 and its lo half for s = 2, Bt
+// its lo half for s = 1 and its hi half otherwise.
+struct Tf32x3Operands {
+  using T = float;
+  static constexpr int kStep = 32;
+  static constexpr int kSegments = 3;
+  static constexpr uint32_t kFormat = 2;  // tf32 (kind::tf32)
+  static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t per) {
+    const int64_t seg = kb / per, j = kb - seg * per;
+    return (int32_t)((seg == 2 ? per + j : j) * kStep);
+  }
+  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t per) {
+    const int64_t seg = kb / per, j = kb - seg * per;
+    return (int32_t)((seg == 1 ? per + j : j) * kStep);
+  }
+};
+
+// The instruction descriptor of an M x BN product with f32 accumulation for operands `Op`.
+template <class Op>
+constexpr uint32_t idesc(int m) {
+  return (1u << 4) | (Op::kFormat << 7) | (Op::kFormat << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
 struct Shared {
   // the operand ring, 1024-byte aligned for the 128-byte swizzle
   alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
@@ -148,6 +201,21 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate));
+}
+
+// One M=128 x N=256 MMA of 32 bytes of K from the operand tiles at adesc, bdesc.
+template <class Op>
+__device__ __forceinline__ void mma_step(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  if constexpr (Op::kFormat == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op>(BM)), "r"(accumulate));
+  } else {
+    mma_bf16(tmem_d, adesc, bdesc, accumulate);
+  }
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -420,17 +488,21 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows
   }
 }
 
-template <class Epi>
-__global__ void __launch_bounds__(THREADS, 1)
-    matmul_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
-                       const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
-                       int64_t k, Epi epi, int32_t* status) {
+// The one-CTA kernel's body, for operands `Op`; `k` is the columns of one operand segment
+// (K for bf16, Kp for tf32x3), a multiple of Op::kStep.
+template <class Op, class Epi>
+__device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
+                                                   const CUtensorMap& map_b, int64_t m,
+                                                   int64_t n, int64_t k, const Epi& epi,
+                                                   int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   Shared& s = *reinterpret_cast<Shared*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t m_blocks = (m + BM - 1) / BM, n_blocks = (n + BN - 1) / BN, k_blocks = k / BK;
+  const int64_t per = k / Op::kStep;  // K-steps per operand segment
+  const int64_t m_blocks = (m + BM - 1) / BM, n_blocks = (n + BN - 1) / BN;
+  const int64_t k_blocks = Op::kSegments * per;
   const int64_t tiles = m_blocks * n_blocks;
 
   if (threadIdx.x == 0) {
@@ -456,6 +528,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // the set-up above overlaps the previous kernel; its results are needed from here on
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -473,8 +548,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           mbar_expect_tx(&s.full[st], STAGE_BYTES);
-          tma_load_2d(s.stage[st], &map_a, &s.full[st], (int32_t)(kb * BK), (int32_t)(mb * BM));
-          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], (int32_t)(kb * BK),
+          tma_load_2d(s.stage[st], &map_a, &s.full[st], Op::a_col(kb, per), (int32_t)(mb * BM));
+          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], Op::b_col(kb, per),
                       (int32_t)(nb * BN));
         }
       }
@@ -506,9 +581,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint64_t bdesc = smem_desc(s.stage[st] + A_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            // advancing K by 16 bf16 = 32 bytes inside the swizzle row: +2 in addr >> 4
-            mma_bf16(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
-                     (kb > 0 || kk > 0) ? 1u : 0u);
+            // advancing K by 32 bytes inside the swizzle row: +2 in addr >> 4
+            mma_step<Op>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
+                         (kb > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&s.empty[st]);
         }
@@ -553,6 +628,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
+                       int64_t k, Epi epi, int32_t* status) {
+  matmul_single_body<Bf16Operands>(map_a, map_b, m, n, k, epi, status);
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
+                         int64_t k, Epi epi, int32_t* status) {
+  matmul_single_body<Tf32x3Operands>(map_a, map_b, m, n, k, epi, status);
+}
+
 // ---- the 2-CTA form: a cluster of two CTAs on two SMs computes 256 x 256 tiles with
 // tcgen05.mma.cta_group::2 (M = 256: each CTA holds 128 rows of A and 128 rows of B^T in its
 // shared memory and 128 rows of the accumulator in its TMEM). Per CTA a K-step moves 32 KB
@@ -568,8 +659,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 constexpr int PAIR_STAGES = 5;
 constexpr int PAIR_B_BYTES = (BN / 2) * BK * 2;
 constexpr int PAIR_STAGE_BYTES = A_BYTES + PAIR_B_BYTES;
-constexpr uint32_t PAIR_IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
-                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
 
 struct PairShared {
   alignas(1024) uint8_t stage[PAIR_STAGES][PAIR_STAGE_BYTES];
@@ -610,13 +699,23 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+// One M=256 x N=256 MMA of 32 bytes of K over the pair (issued by the first CTA).
+template <class Op>
+__device__ __forceinline__ void mma_pair_step(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(PAIR_IDESC), "r"(accumulate));
+  if constexpr (Op::kFormat == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op>(2 * BM)), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op>(2 * BM)), "r"(accumulate));
+  }
 }
 
 // Arrive on `bar` (same offset) in both CTAs of the pair once this thread's MMAs are done.
@@ -638,11 +737,12 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
-template <class Epi>
-__global__ void __launch_bounds__(THREADS, 1)
-    matmul_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a,
-                            const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
-                            int64_t k, Epi epi, int32_t* status) {
+// The 2-CTA kernel's body, for operands `Op` (`k` as for matmul_single_body).
+template <class Op, class Epi>
+__device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
+                                                 const CUtensorMap& map_b, int64_t m,
+                                                 int64_t n, int64_t k, const Epi& epi,
+                                                 int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   PairShared& s = *reinterpret_cast<PairShared*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -652,7 +752,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const bool first = rank == 0;
   const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
   const int64_t m_blocks = (m + 2 * BM - 1) / (2 * BM), n_blocks = (n + BN - 1) / BN;
-  const int64_t k_blocks = k / BK, tiles = m_blocks * n_blocks;
+  const int64_t per = k / Op::kStep;  // K-steps per operand segment
+  const int64_t k_blocks = Op::kSegments * per, tiles = m_blocks * n_blocks;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PAIR_STAGES; ++i) {
@@ -679,6 +780,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   cluster_sync();  // the barriers of both CTAs exist before any load or commit reaches them
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // the set-up above overlaps the previous kernel; its results are needed from here on
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -697,9 +801,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           if (first) mbar_expect_tx(&s.full[st], 2 * PAIR_STAGE_BYTES);
           const uint32_t bar = mapa_shared(smem_u32(&s.full[st]), 0);
-          tma_load_2d_pair(s.stage[st], &map_a, bar, (int32_t)(kb * BK),
+          tma_load_2d_pair(s.stage[st], &map_a, bar, Op::a_col(kb, per),
                            (int32_t)(mb * 2 * BM + rank * BM));
-          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, (int32_t)(kb * BK),
+          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, Op::b_col(kb, per),
                            (int32_t)(nb * BN + rank * (BN / 2)));
         }
       }
@@ -735,8 +839,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t bdesc = smem_desc(s.stage[st] + A_BYTES);
 #pragma unroll
             for (int kk = 0; kk < BK / UMMA_K; ++kk)
-              mma_bf16_pair(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
-                            (kb > 0 || kk > 0) ? 1u : 0u);
+              mma_pair_step<Op>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
+                                (kb > 0 || kk > 0) ? 1u : 0u);
             mma_commit_pair(&s.empty[st]);
           }
           if (ok) mma_commit_pair(&s.acc_full[a]);
@@ -781,6 +885,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                            const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
+                            int64_t k, Epi epi, int32_t* status) {
+  matmul_pair_body<Bf16Operands>(map_a, map_b, m, n, k, epi, status);
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                              const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
+                              int64_t k, Epi epi, int32_t* status) {
+  matmul_pair_body<Tf32x3Operands>(map_a, map_b, m, n, k, epi, status);
+}
+
 // ---- host side
 
 using ppyb200::DeviceOnce;
@@ -806,16 +926,19 @@ inline EncodeTiled encode_tiled() {
   return fn;
 }
 
-// A row-major [rows, k] bf16 matrix as a TMA map of [box_rows, 64] tiles, 128-byte swizzle.
-inline bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+// A row-major [rows, cols] matrix of Op::T as a TMA map of [box_rows, Op::kStep] tiles (one
+// 128-byte swizzle row wide), 128-byte swizzle.
+template <class Op>
+inline bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                     int box_rows) {
   EncodeTiled encode = encode_tiled();
   if (encode == nullptr) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(cols * (int64_t)sizeof(typename Op::T))};
+  const cuuint32_t box[2] = {(cuuint32_t)Op::kStep, (cuuint32_t)box_rows};
   const cuuint32_t elem[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  return encode(map, Op::kMapType, 2, const_cast<void*>(base), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -829,21 +952,37 @@ inline bool tileable(int64_t m, int64_t n, int64_t k) {
 
 inline size_t shared_bytes() { return sizeof(Shared) + 1024; }
 
-// The one-CTA kernel on `stream`; returns a cudaError_t (cudaErrorInvalidValue when the maps
-// cannot be made). The caller checks `tileable` and 16-byte alignment of a, bt first.
+// The __global__ kernels of operands `Op` with epilogue `Epi`.
+template <class Op, class Epi>
+struct Kernels;
 template <class Epi>
-inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m,
-                                 int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
-                                 cudaStream_t stream) {
+struct Kernels<Bf16Operands, Epi> {
+  static constexpr auto single = matmul_bf16_kernel<Epi>;
+  static constexpr auto pair = matmul_bf16_pair_kernel<Epi>;
+};
+template <class Epi>
+struct Kernels<Tf32x3Operands, Epi> {
+  static constexpr auto single = matmul_tf32x3_kernel<Epi>;
+  static constexpr auto pair = matmul_tf32x3_pair_kernel<Epi>;
+};
+
+// The one-CTA kernel on `stream` over operand matrices a [m, Op::kSegments > 1 ? 2k : k] and
+// bt [n, same] (see the operand structs); returns a cudaError_t (cudaErrorInvalidValue when
+// the maps cannot be made). The caller checks the shapes and 16-byte alignment of a, bt.
+template <class Op, class Epi>
+inline cudaError_t launch_single_op(const typename Op::T* a, const typename Op::T* bt, int64_t m,
+                                    int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
+                                    cudaStream_t stream) {
+  const int64_t cols = Op::kSegments > 1 ? 2 * k : k;
   CUtensorMap map_a, map_b;
-  if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN))
+  if (!make_map<Op>(&map_a, a, m, cols, BM) || !make_map<Op>(&map_b, bt, n, cols, BN))
     return cudaErrorInvalidValue;
   static DeviceOnce configured;
   int ready = 0;
   cudaError_t e = configured.get(
       [](int* v) {
         *v = 1;
-        return cudaFuncSetAttribute(matmul_bf16_kernel<Epi>,
+        return cudaFuncSetAttribute(Kernels<Op, Epi>::single,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)shared_bytes());
       },
@@ -851,9 +990,8 @@ inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt
   if (e != cudaSuccess) return e;
   const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = (int)(tiles < sm_count ? tiles : sm_count);
-  matmul_bf16_kernel<Epi><<<grid, THREADS, shared_bytes(), stream>>>(map_a, map_b, m, n, k, epi,
-                                                                     status);
-  return cudaGetLastError();
+  return launch_pdl(Kernels<Op, Epi>::single, dim3(grid), dim3(THREADS), shared_bytes(), stream,
+                    map_a, map_b, m, n, k, epi, status);
 }
 
 inline size_t pair_shared_bytes() { return sizeof(PairShared) + 1024; }
@@ -864,21 +1002,24 @@ constexpr int64_t DEEP_K = 2048;
 
 
 // The 2-CTA kernel on `stream`: clusters of two CTAs, as many as can be resident at once (at
-// most one per 256 x 256 tile). Same contract as `launch`.
-template <class Epi>
-inline cudaError_t launch_pair(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m,
-                               int64_t n, int64_t k, Epi epi, int32_t* status,
-                               cudaStream_t stream) {
+// most one per 256 x 256 tile). Same contract as `launch_single_op`.
+template <class Op, class Epi>
+inline cudaError_t launch_pair_op(const typename Op::T* a, const typename Op::T* bt, int64_t m,
+                                  int64_t n, int64_t k, Epi epi, int32_t* status,
+                                  cudaStream_t stream) {
+  const int64_t cols = Op::kSegments > 1 ? 2 * k : k;
   CUtensorMap map_a, map_b;
-  if (!make_map(&map_a, a, m, k, BM) || !make_map(&map_b, bt, n, k, BN / 2))
+  if (!make_map<Op>(&map_a, a, m, cols, BM) || !make_map<Op>(&map_b, bt, n, cols, BN / 2))
     return cudaErrorInvalidValue;
   static DeviceOnce resident;
   cudaLaunchConfig_t config = {};
-  cudaLaunchAttribute attribute[1];
+  cudaLaunchAttribute attribute[2];
   attribute[0].id = cudaLaunchAttributeClusterDimension;
   attribute[0].val.clusterDim.x = 2;
   attribute[0].val.clusterDim.y = 1;
   attribute[0].val.clusterDim.z = 1;
+  attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[1].val.programmaticStreamSerializationAllowed = 1;
   config.blockDim = dim3(THREADS, 1, 1);
   config.dynamicSmemBytes = pair_shared_bytes();
   config.stream = stream;
@@ -889,25 +1030,32 @@ inline cudaError_t launch_pair(const __nv_bfloat16* a, const __nv_bfloat16* bt, 
   int max_clusters = 0;
   cudaError_t e = resident.get(
       [&config](int* v) {
-        cudaError_t r = cudaFuncSetAttribute(matmul_bf16_pair_kernel<Epi>,
+        cudaError_t r = cudaFuncSetAttribute(Kernels<Op, Epi>::pair,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)pair_shared_bytes());
         if (r != cudaSuccess) return r;
         cudaLaunchConfig_t probe = config;
         probe.gridDim = dim3(2, 1, 1);
-        return cudaOccupancyMaxActiveClusters(v, matmul_bf16_pair_kernel<Epi>, &probe);
+        return cudaOccupancyMaxActiveClusters(v, Kernels<Op, Epi>::pair, &probe);
       },
       &max_clusters);
   if (e != cudaSuccess) return e;
   const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
   const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
   config.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-  return cudaLaunchKernelEx(&config, matmul_bf16_pair_kernel<Epi>, map_a, map_b, m, n, k, epi,
-                            status);
+  config.numAttrs = ppyb200_pdl() ? 2 : 1;
+  return cudaLaunchKernelEx(&config, Kernels<Op, Epi>::pair, map_a, map_b, m, n, k, epi, status);
 }
 
-// The tensor-core GEMM: CTA pairs or one CTA per tile, as ppyb200_gemm_form() says (by K by
-// default). Same contract as `launch_single`.
+template <class Epi>
+inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m,
+                                 int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
+                                 cudaStream_t stream) {
+  return launch_single_op<Bf16Operands>(a, bt, m, n, k, epi, status, sm_count, stream);
+}
+
+// The tensor-core GEMM: CTA pairs or one CTA per tile, as ppyb200_gemm_form() says (by shape
+// by default), over bf16 A [m, k] and Bt [n, k]. Same contract as `launch_single_op`.
 template <class Epi>
 inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64_t m, int64_t n,
                           int64_t k, Epi epi, int32_t* status, int sm_count,
@@ -919,8 +1067,8 @@ inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64
   // 1.35, FC 1.92 against 1.95 per forward; K = 3072 and 8192: 3 % and 2.4 %). Below 256
   // rows half of each pair would idle.
   if (form == PPYB200_GEMM_PAIRS || (form == PPYB200_GEMM_BY_SHAPE && m >= 2 * BM))
-    return launch_pair(a, bt, m, n, k, epi, status, stream);
-  return launch_single(a, bt, m, n, k, epi, status, sm_count, stream);
+    return launch_pair_op<Bf16Operands>(a, bt, m, n, k, epi, status, stream);
+  return launch_single_op<Bf16Operands>(a, bt, m, n, k, epi, status, sm_count, stream);
 }
 
 }  // namespace gemm

@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const int64_t* __restrict__ 
                                                     float* __restrict__ x, int64_t tokens,
                                                     int64_t length, int64_t width,
                                                     int64_t vocab, int32_t* status) {
+  ppyb200::pdl_wait();  // the previous kernel may still read x
   const int64_t groups = width / 8;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= tokens * groups) return;
@@ -307,10 +308,11 @@ int32_t ppyb200_gpt2_embed(const int64_t* ids, const uint16_t* wte, const uint16
     return PPYB200_RAISED;
   }
   const int64_t work = tokens * (width / 8);
-  embed_kernel<<<(unsigned)((work + 255) / 256), 256, 0, stream_now()>>>(
-      ids, reinterpret_cast<const __nv_bfloat16*>(wte), reinterpret_cast<const __nv_bfloat16*>(wpe),
-      x, tokens, length, width, vocab, status);
-  return finish(cudaGetLastError(), "ppyb200_gpt2_embed", 1);
+  const cudaError_t e = ppyb200::launch_pdl(
+      embed_kernel, dim3((unsigned)((work + 255) / 256)), dim3(256), 0, stream_now(), ids,
+      reinterpret_cast<const __nv_bfloat16*>(wte), reinterpret_cast<const __nv_bfloat16*>(wpe), x,
+      tokens, length, width, vocab, status);
+  return finish(e, "ppyb200_gpt2_embed", 1);
 }
 
 int32_t ppyb200_linear_bf16(const uint16_t* a, const uint16_t* w, const float* bias,

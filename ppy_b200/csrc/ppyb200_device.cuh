@@ -21,6 +21,9 @@
 
 #include <atomic>
 #include <mutex>
+#include <utility>
+
+extern "C" int32_t ppyb200_pdl(void);  // libppyb200: whether launches carry the PDL attribute
 
 #define PPY_STATUS_OK 0
 #define PPY_STATUS_FALLBACK 1
@@ -291,6 +294,22 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(PENDING) : "memory");
 }
 
+// ---- programmatic dependent launch (sm_90 and later)
+//
+// A kernel launched with the programmatic-serialization attribute (launch_pdl below) may
+// start while the kernel before it on the stream is still running, once every CTA of that
+// kernel has run pdl_trigger() or exited: its CTAs then set up (barriers, tensor memory)
+// while the previous kernel drains. Such a kernel runs pdl_wait() -- which returns when the
+// previous kernel has completed and its memory operations are visible -- before it reads or
+// writes any global memory, and every kernel that runs pdl_wait() first has done so
+// transitively for all the work before it. A kernel launched without the attribute, or
+// after one that never triggers, starts as usual after the previous one completes, and
+// pdl_wait() returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- host side
 
 // A value set up once per device for one kernel (its shared-memory attribute, its resident
@@ -324,5 +343,23 @@ struct DeviceOnce {
     return cudaSuccess;
   }
 };
+
+// Launch `kernel` on `stream` with the programmatic-serialization attribute while
+// ppyb200_pdl() is on. The kernel runs pdl_wait() before it touches global memory.
+template <class... Params, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = ppyb200_pdl() ? 1 : 0;
+  return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace ppyb200

@@ -47,6 +47,7 @@ std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
 std::atomic<uint64_t> g_launches{0};
 std::atomic<uint64_t> g_allocations{0};  // cudaMalloc calls that succeeded
+std::atomic<int32_t> g_pdl{1};            // launches carry the PDL attribute
 
 // cudaMalloc, counted (ppyb200_device_allocations).
 cudaError_t counted_malloc(void** pointer, size_t bytes) {
@@ -305,6 +306,12 @@ int32_t ppyb200_check(int32_t cuda_error, const char* what) {
 uint64_t ppyb200_launches(void) { return g_launches.load(); }
 
 uint64_t ppyb200_device_allocations(void) { return g_allocations.load(); }
+
+int32_t ppyb200_set_pdl(int32_t enabled) {
+  return g_pdl.exchange(enabled != 0 ? 1 : 0);
+}
+
+int32_t ppyb200_pdl(void) { return g_pdl.load(std::memory_order_relaxed); }
 
 void ppyb200_count_launches(uint64_t count) { g_launches.fetch_add(count); }
 

@@ -2,8 +2,9 @@
 that follows it (the bias add FuseTensor leaves) fused into the epilogue.
 
 bf16 operands with K a multiple of 64 run on the tcgen05 kernel (csrc/gemm_sm100.cuh)
-after B, row-major [K, N] as the IR has it, is transposed into the scratch arena; every
-other case runs on the CUDA-core kernel (csrc/gemm_simt.cuh). The epilogue is a functor
+after B, row-major [K, N] as the IR has it, is transposed into the scratch arena; f32
+operands run on the same kernel as three tf32 products after a split pass into the arena
+(csrc/gemm_f32.cuh); every other case runs on the CUDA-core kernel (csrc/gemm_simt.cuh). The epilogue is a functor
 generated from the group's element program: input 0 is the product's element, the other
 inputs are read per row, per column, per element or once.
 """
@@ -91,7 +92,18 @@ def matmul_launch(kernel: P.MatmulKernel, fn: P.TensorFunction, src) -> dict:
              f"  {name}_epi epi{{{init}}};",
              "  if (m > 0) {"]
     tensor_cores = a.dtype == "bf16" and kernel.k % 64 == 0
-    if tensor_cores:
+    tf32x3 = a.dtype == "f32" and b.dtype == "f32"
+    if tf32x3:
+        lines += [
+            "    // f32 operands: three tf32 products on the tensor cores (gemm_f32.cuh); the",
+            "    // split operands and the non-finite flag live in the scratch arena",
+            "    float* work = (float*)ppyb200_scratch_take(&scratch, ppyb200::gemm::tf32x3_work_bytes(m, n, k));",
+            "    if (work == nullptr) return PPY_STATUS_RAISED;",
+            f"    cudaError_t e = ppyb200::gemm::launch_tf32x3((const float*){a.pointer}, (const float*){b.pointer}, "
+            "work, m, n, k, epi, status, ppyb200_sm_count(), stream);",
+            f"    if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
+            "    launches += 4;"]
+    elif tensor_cores:
         lines += [
             f"    if (ppyb200_aligned({a.pointer}, 16) && m < (1ll << 31)) {{",
             "      // B is row-major [K, N]; the tensor-core kernel reads it K-major [N, K]",
@@ -113,7 +125,10 @@ def matmul_launch(kernel: P.MatmulKernel, fn: P.TensorFunction, src) -> dict:
             f"    if (e != cudaSuccess) return ppyb200_check((int32_t)e, \"{name}\");",
             "    launches += 1;"]
     lines += ["  }", "}"]
-    info = {"launch": lines, "status": tensor_cores, "gemm": True}
+    info = {"launch": lines, "status": tensor_cores or tf32x3, "gemm": True}
     if tensor_cores:
         info["scratch"] = f"ppyb200_round256((int64_t){kernel.n} * {kernel.k} * 2)"
+    elif tf32x3:
+        info["scratch"] = (f"ppyb200::gemm::tf32x3_work_bytes({m_expr}, (int64_t){kernel.n}, "
+                           f"(int64_t){kernel.k})")
     return info

@@ -578,6 +578,11 @@ def golden_matmul() -> None:
     module = build_matmul_bf16(k=8192, n=8192)
     module.name = "matmul_bf16_8192"
     write_ppyir(shared_passes(module, False), "matmul_bf16_8192")
+    # the fp32-input variant's benchmark shape: M = N = K = 4096 (M bound at run time); its
+    # IR only (the reference's naive loop nest would take hours at this size)
+    module = build_matmul(k=4096, n=4096)
+    module.name = "matmul_f32_4096"
+    write_ppyir(shared_passes(module, False), "matmul_f32_4096")
 
 
 COLLATZ = '''

@@ -202,13 +202,24 @@ def test_transpose(lib):
 
 
 def test_bench_size_matmul_properties(lib):
-    """8192^3 (the benchmark shape): spot rows against float64, and linearity in B."""
+    """8192^3 (the benchmark shape): the whole output against an f32 matmul of the same
+    bf16-rounded operands (cuBLAS, TF32 off), spot rows against float64, and linearity in B."""
     m = n = k = 8192
     a, b, bias = _operands(m, n, k, seed=3)
     da, db, dbias = a.cuda(), b.cuda(), bias.cuda()
     out = torch.empty((m, n), device="cuda")
     assert lib.ppyb200_matmul_bf16(_ptr(da), _ptr(db), _ptr(dbias), _ptr(out), m, n, k) == 0
     torch.cuda.synchronize()
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        whole = torch.addmm(dbias, da.float(), db.float())
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+    scale = torch.maximum(whole.abs(), whole.pow(2).mean().sqrt())
+    worst = float(((out - whole).abs() / scale).max())
+    assert worst <= 1e-4, worst  # two f32 accumulations of the same products, other orders
+    del whole, scale
     rows = torch.tensor([0, 1, 127, 128, 4095, 8191])
     ref = (a[rows].double() @ b.double() + bias.double()).numpy()
     _check(out[rows.cuda()], ref, rel=1e-4)
@@ -267,3 +278,96 @@ def test_bench_shape_module_rows(lib):
     assert module.device.matmul_bias_bf16(da, db, dbias, out).status == 0
     torch.cuda.synchronize()
     _check(out, _reference(a, b, bias), rel=1e-4)
+
+
+# ---------------------------------------------------------------- f32 operands (three tf32 products)
+#
+# ppyb200_matmul_f32 computes A_hi B_hi + A_hi B_lo + A_lo B_hi on the tensor cores (x_hi = x
+# rounded to tf32, x_lo = the rest rounded to tf32). Tolerance: the north star's 1e-5 relative
+# for fp32 reductions, per element against max(|ref|, rms(ref)) of a float64 evaluation.
+
+
+def _f32_operands(m, n, k, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(m, k, device="cuda", generator=g) / max(k, 1) ** 0.5
+    b = torch.randn(k, n, device="cuda", generator=g) / max(k, 1) ** 0.5
+    bias = 0.02 * torch.randn(n, device="cuda", generator=g)
+    return a, b, bias
+
+
+def _matmul_f32(lib, a, b, bias, m, n, k):
+    lib.ppyb200_matmul_f32.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+    lib.ppyb200_matmul_f32.restype = ctypes.c_int32
+    c = torch.full((m, n), float("nan"), device="cuda")
+    assert lib.ppyb200_matmul_f32(_ptr(a), _ptr(b), _ptr(bias), _ptr(c), m, n, k) == 0
+    torch.cuda.synchronize()
+    return c
+
+
+def _f32_reference(a, b, bias):
+    ref = a.double() @ b.double()
+    return ref + bias.double() if bias is not None else ref
+
+
+def _check_f32(c, ref, rel=1e-5):
+    scale = torch.maximum(ref.abs(), ref.pow(2).mean().sqrt())
+    err = float(((c.double() - ref).abs() / scale).max())
+    assert err <= rel, err
+    return err
+
+
+def test_f32_matmul_4096_cube_against_float64(lib):
+    """The fp32-input variant at its benchmark size, whole output against float64."""
+    m = n = k = 4096
+    a, b, bias = _f32_operands(m, n, k, seed=1)
+    c = _matmul_f32(lib, a, b, bias, m, n, k)
+    _check_f32(c, _f32_reference(a, b, bias))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (100, 200, 50), (300, 513, 77), (257, 255, 1000),
+                                   (64, 96, 80), (1024, 1024, 4096)])
+def test_f32_matmul_ragged_shapes(lib, m, n, k):
+    a, b, bias = _f32_operands(m, n, k, seed=2)
+    c = _matmul_f32(lib, a, b, bias, m, n, k)
+    _check_f32(c, _f32_reference(a, b, bias))
+
+
+def test_f32_matmul_empty_k_gives_the_bias(lib):
+    _, _, bias = _f32_operands(64, 96, 1, seed=3)
+    a = torch.empty(64, 0, device="cuda")
+    b = torch.empty(0, 96, device="cuda")
+    c = _matmul_f32(lib, a, b, bias, 64, 96, 0)
+    assert torch.equal(c, bias.expand(64, 96))
+
+
+@pytest.mark.parametrize("form", [1, 2])
+def test_f32_matmul_pairs_and_single_ctas_agree(lib, form):
+    m, n, k = 512, 768, 1024
+    a, b, bias = _f32_operands(m, n, k, seed=4)
+    before = lib.ppyb200_set_gemm_form(form)
+    try:
+        c = _matmul_f32(lib, a, b, bias, m, n, k)
+    finally:
+        lib.ppyb200_set_gemm_form(before)
+    _check_f32(c, _f32_reference(a, b, bias))
+
+
+def test_f32_matmul_non_finite_inputs_follow_ieee(lib):
+    """An infinity or a NaN among the inputs: C is recomputed with f32 FMAs, so infinities
+    stay infinities (a tf32 split would give NaN where inf meets a zero low part)."""
+    m, n, k = 96, 130, 70
+    a, b, bias = _f32_operands(m, n, k, seed=5)
+    b = b.abs() + 0.25  # positive columns: inf * b keeps its sign
+    a[3, 10] = float("inf")
+    a[7, 0] = float("-inf")
+    a[11, 5] = float("nan")
+    c = _matmul_f32(lib, a, b, bias, m, n, k)
+    ref = _f32_reference(a, b, bias)
+    assert torch.equal(torch.isnan(c), torch.isnan(ref))
+    assert torch.equal(torch.isinf(c), torch.isinf(ref))
+    inf = torch.isinf(ref)
+    assert torch.equal(torch.sign(c[inf]), torch.sign(ref[inf]).float())
+    finite = torch.isfinite(ref)
+    scale = ref[finite].pow(2).mean().sqrt()
+    assert float(((c[finite].double() - ref[finite]).abs() / torch.maximum(
+        ref[finite].abs(), scale)).max()) <= 1e-5
