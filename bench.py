@@ -619,37 +619,69 @@ class Gpt2(Workload):
         from ppy_b200 import gpt2
 
         self.gpt2 = gpt2
+        self.torch = torch
         self.model = gpt2.GPT2(gpt2.GPT2_124M, seed=0)
         b = self.ids.shape[0]
-        stream = torch.cuda.current_stream()
+        self.stream = torch.cuda.current_stream()
         if self.eager:
             self.dids = self.ids.cuda()
             self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
+            self.slots = [(self.dids, self.logits, None)]
         else:
-            self.graphed = self.model.graphed(b, self.LENGTH, stream)
-            self.dids = self.graphed.ids
-            self.dids.copy_(self.ids)
-            self.logits = self.graphed.logits
+            # two captured forwards over their own ids and logits buffers (the activations
+            # are shared: the replays run one after another on the stream), so that one
+            # step's logits can go out over PCIe while the next step computes
+            self.slots = []
+            for _ in range(2):
+                graphed = self.model.graphed(b, self.LENGTH, self.stream)
+                graphed.ids.copy_(self.ids)
+                self.slots.append((graphed.ids, graphed.logits, graphed))
+            self.dids, self.logits, self.graphed = self.slots[0]
         self.pids = self.ids.pin_memory()
-        self.host_logits = torch.empty(b, self.LENGTH, VOCAB).pin_memory()
+        self.host_logits = [torch.empty(b, self.LENGTH, VOCAB).pin_memory()
+                            for _ in self.slots]
+        self.copy_stream = torch.cuda.Stream()
+        self.computed = [torch.cuda.Event() for _ in self.slots]
+        self.copied = [torch.cuda.Event() for _ in self.slots]
+        self.turn = 0
         self.runtime = runtime
 
-    def _forward(self):
-        if self.eager:
-            self.model.forward(self.dids, self.logits)
+    def _forward(self, slot=0):
+        ids, logits, graphed = self.slots[slot]
+        if graphed is None:
+            self.model.forward(ids, logits)
         else:
-            self.graphed.run()
+            graphed.run()
 
     def step_device(self):
         self._forward()
         return 0
 
     def step_host(self):
-        # e2e: the ids from pinned host memory in, every logit out into a contiguous host array
-        self.dids.copy_(self.pids, non_blocking=True)
-        self._forward()
-        self.runtime.copy_rows_to_host(self.host_logits, self.logits)
+        """e2e: the step's ids from pinned host memory in, every logit out into a contiguous
+        pinned host array. Steps alternate between the two buffer sets; the logits of a step
+        go out on a copy stream while the next step computes, and a buffer set is reused
+        only after its previous copy-out finished."""
+        torch = self.torch
+        slot = self.turn % len(self.slots)
+        self.turn += 1
+        ids, logits, _ = self.slots[slot]
+        self.stream.wait_event(self.copied[slot])  # this set's last copy-out is done
+        ids.copy_(self.pids, non_blocking=True)
+        self._forward(slot)
+        self.computed[slot].record(self.stream)
+        with torch.cuda.stream(self.copy_stream):
+            self.copy_stream.wait_event(self.computed[slot])
+            self.runtime.set_stream(self.copy_stream)
+            self.runtime.copy_rows_to_host(self.host_logits[slot], logits)
+            self.runtime.set_stream(self.stream)
+            self.copied[slot].record(self.copy_stream)
         return 0
+
+    def drain(self):
+        """The end of the timed host-memory steps waits for the last copy-outs."""
+        for event in self.copied:
+            self.stream.wait_event(event)
 
     def finish(self) -> int:
         return self.model.status()
@@ -692,9 +724,11 @@ class Gpt2(Workload):
         return float(self.LENGTH)
 
     def compare(self) -> float:
-        """Max error of sequence 0's logits against the CPU forward, per element against
-        max(|ref|, rms of ref): the 2e-2 bf16 tolerance's measure."""
-        got = self.logits[0].cpu().double()
+        """Max error of sequence 0's logits, as the last host-memory step copied them out,
+        against the CPU forward, per element against max(|ref|, rms of ref)."""
+        self.torch.cuda.synchronize()
+        slot = (self.turn - 1) % len(self.slots)
+        got = self.host_logits[slot][0].double()
         ref = self.cpu_out[0].double()
         scale = torch_max(ref.abs(), ref.pow(2).mean().sqrt())
         return float(((got - ref).abs() / scale).max())
@@ -754,14 +788,24 @@ class Gpt2TP(Gpt2):
         self.model = gpt2_tp.GPT2TensorParallel(gpt2.GPT2_124M, seed=0, group=group,
                                                 exchange=self.exchange)
         self.gpt2 = gpt2
+        self.torch = torch
         self.eager = True
+        self.stream = torch.cuda.current_stream()
         self.dids = self.ids.cuda()
         self.pids = self.ids.pin_memory()
         v0, v1 = self.model.shard.vocab
         b = self.ids.shape[0]
         self.logits = self.model.new_logits(b, self.LENGTH)  # rows on 128-byte lines
-        self.host_logits = torch.empty(b, self.LENGTH, v1 - v0).pin_memory()
+        self.slots = [(self.dids, self.logits, None)]
+        self.host_logits = [torch.empty(b, self.LENGTH, v1 - v0).pin_memory()]
+        self.copy_stream = torch.cuda.Stream()
+        self.computed = [torch.cuda.Event()]
+        self.copied = [torch.cuda.Event()]
+        self.turn = 0
         self.runtime = runtime
+
+    def _forward(self, slot=0):
+        self.model.forward(self.dids, self.logits)
 
     def job_units(self) -> float:
         return float(self.units()) * self.dp  # the ranks of a group share their tokens
@@ -782,7 +826,8 @@ class Gpt2TP(Gpt2):
 
     def compare(self) -> float:
         v0, v1 = self.model.shard.vocab
-        got = self.logits[0].cpu().double()
+        self.torch.cuda.synchronize()
+        got = self.host_logits[0][0].double()
         ref = self.cpu_out[0, :, v0:v1].double()
         scale = torch_max(ref.abs(), ref.pow(2).mean().sqrt())
         return float(((got - ref).abs() / scale).max())
@@ -897,6 +942,8 @@ def measure(w: Workload, steps: int, warmup: int, dist: Dist, stream, runtime, t
         for _ in range(steps):
             if step() != 0:
                 raise SystemExit(f"{w.name}: a step failed")
+        if getattr(w, "drain", None) is not None:
+            w.drain()  # work the steps left on other streams ends inside the timed region
         end.record(stream)
         torch.cuda.synchronize()
         dist.barrier()

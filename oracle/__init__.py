@@ -211,3 +211,36 @@ def fold_axes(values: np.ndarray, kind: str, axes: tuple, keepdims: bool, dtype)
     if keepdims:
         out = out.reshape(tuple(1 if d in axes else values.shape[d] for d in range(values.ndim)))
     return out
+
+
+# -- parallel bodies that call the math externs (tests/golden/parallel_math.*) ---------------
+
+
+def math_table(lo: int, hi: int) -> np.ndarray:
+    """out[i - lo] = tanh(x) + erf(x) + atan2(x, 1.5), x = (i - 500) * 0.01, in CPython: the
+    plain run of the fixture's `math_table`. The reference's native path calls the same libm
+    functions through ppy_math_unary/binary (src/ppy_runtime/stdlib.c:497-528), left to
+    right, so the two agree bit for bit on one machine."""
+    import math
+
+    out = np.empty(max(hi - lo, 0), np.float64)
+    for i in range(lo, hi):
+        x = (i - 500) * 0.01
+        out[i - lo] = math.tanh(x) + math.erf(x) + math.atan2(x, 1.5)
+    return out
+
+
+def asin_table(lo: int, hi: int) -> tuple[int, np.ndarray]:
+    """(status, out) for the fixture's `asin_table`: out[i - lo] = asin(i * 0.25). A value
+    outside [-1, 1] makes CPython raise ValueError; the native path's domain guard around
+    ppy_math_unary (lowering/stdlib.py:693-731) returns STATUS_FALLBACK so that CPython reruns
+    the call and raises. Status 0 with the values otherwise."""
+    import math
+
+    out = np.empty(max(hi - lo, 0), np.float64)
+    for i in range(lo, hi):
+        x = i * 0.25
+        if not -1.0 <= x <= 1.0:
+            return STATUS_FALLBACK, out
+        out[i - lo] = math.asin(x)
+    return STATUS_OK, out

@@ -1,8 +1,8 @@
 // Causal attention on Blackwell tensor cores, head_dim 64, bf16 in and out, f32 softmax.
 //
 // One persistent CTA per SM walks work items (batch, head, pair of 128-query tiles), heaviest
-// (last) pairs first. The two query tiles of a pair share one stream of key tiles (128 keys
-// each); per key tile and query tile t:
+// (last) pairs first, dealt to the CTAs in a snake order (snake_item). The two query tiles of
+// a pair share one stream of key tiles (128 keys each); per key tile and query tile t:
 //   S_t = Q_t K^T    tcgen05.mma M=128 N=128 K=64 into TMEM (128 columns per query tile)
 //   softmax          warpgroup t (4 warps), one query row per thread: tcgen05.ld of its S row,
 //                    causal mask on the diagonal tile, P = 2^((S - m) * scale * log2 e) rounded
@@ -229,6 +229,17 @@ __device__ __forceinline__ Item item_of(int64_t i, int64_t bh, int64_t heads, in
   return it;
 }
 
+// This CTA's item of round `round`: round r covers items [r G, (r + 1) G) of the heaviest-first
+// order (G = gridDim.x), CTA c taking the c-th of them in even rounds and the (G - 1 - c)-th in
+// odd ones. The CTAs that drew the heaviest items of one round draw the lightest of the next,
+// as a longest-first greedy schedule would: with 4 sequences of 1024 tokens (192 items of 15,
+// 11, 7 and 3 key tiles for 148 SMs) the busiest CTA walks 15 key tiles instead of 18. Every
+// role of the CTA walks the same sequence; an index past the items ends it.
+__device__ __forceinline__ int64_t snake_item(int64_t round) {
+  const int64_t g = gridDim.x, c = blockIdx.x;
+  return round * g + ((round & 1) ? g - 1 - c : c);
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     causal_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_vt,
                   __nv_bfloat16* __restrict__ out, int64_t batch, int64_t length, int64_t heads,
@@ -278,7 +289,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---- loader
       uint64_t kv = 0, qi = 0;
       bool ok = true;
-      for (int64_t i = blockIdx.x; i < items && ok; i += gridDim.x, ++qi) {
+      int64_t round = 0;
+      for (int64_t i = snake_item(0); i < items && ok; i = snake_item(++round), ++qi) {
         const Item it = item_of(i, bh, heads, q_tiles);
         const int32_t row0 = (int32_t)(it.b * length);
         const int q_count = it.has1 ? 2 : 1;
@@ -315,7 +327,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint64_t kv = 0, qi = 0;
       uint64_t sc[2] = {0, 0}, pc[2] = {0, 0};  // S and PV products issued per query tile
       bool ok = true;
-      for (int64_t i = blockIdx.x; i < items && ok; i += gridDim.x, ++qi) {
+      int64_t round = 0;
+      for (int64_t i = snake_item(0); i < items && ok; i = snake_item(++round), ++qi) {
         const Item it = item_of(i, bh, heads, q_tiles);
         const int64_t n_t[2] = {2 * it.p + 1, it.has1 ? 2 * it.p + 2 : 0};
         const int64_t tiles = it.has1 ? n_t[1] : n_t[0];
@@ -393,7 +406,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint64_t scale2 = f2(scale_log2, scale_log2);
     uint64_t sc = 0, pc = 0;
     bool ok = true;
-    for (int64_t i = blockIdx.x; i < items && ok; i += gridDim.x) {
+    int64_t round = 0;
+    for (int64_t i = snake_item(0); i < items && ok; i = snake_item(++round)) {
       const Item it = item_of(i, bh, heads, q_tiles);
       if (t == 1 && !it.has1) continue;
       const int64_t qt = 2 * it.p + t;

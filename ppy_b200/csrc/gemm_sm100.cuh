@@ -71,12 +71,13 @@ struct Bf16Operands {
   using T = __nv_bfloat16;
   static constexpr int kStep = 64;
   static constexpr int kSegments = 1;
+  static constexpr bool kChunked = false;  // one accumulation per tile, over all of K
   static constexpr uint32_t kFormat = 1;  // bf16 (kind::f16)
   static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t) {
+  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t, int64_t) {
     return (int32_t)(kb * kStep);
   }
-  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t) {
+  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t, int64_t) {
     return (int32_t)(kb * kStep);
   }
 };
@@ -86,25 +87,42 @@ struct Bf16Operands {
 // and x_lo is (x - x_hi) rounded to tf32: what is dropped is A_lo.B_lo and the third
 // 11-bit piece of each operand, both about 2^-22 of |a||b| (fp32 keeps 24 bits). The
 // operands are A2 [M, 2 Kp] = [A_hi | A_lo] and B2t [N, 2 Kp] = [B_hi^T | B_lo^T] (Kp = K
-// rounded up to 32, zero-filled), written by split_tf32 below; the kernel's K-steps walk
-// the three products back to back as one tf32 product of depth 3 Kp: for step kb of
-// segment s = kb / (Kp/32), A reads its hi half for s = 0, 1 and its lo half for s = 2, Bt
-// its lo half for s = 1 and its hi half otherwise.
+// rounded up to 32, zero-filled), written by the split in gemm_f32.cuh.
+//
+// The tensor core adds each MMA's products into the f32 accumulator with a truncation whose
+// errors do not cancel: over n MMAs they grow like n * 2^-24 of the sum (measured: 1.5e-4 of
+// the rms at K = 4096 when the three products ran back to back, the small ones added last to
+// the full-size sum). So K is walked in chunks of cs 32-wide steps (cs = the largest divisor
+// of Kp/32 up to 8: 256 columns): each chunk's A_lo.B_hi, then A_hi.B_lo, then A_hi.B_hi go
+// into a fresh accumulator -- the small products first, while the sum is small -- and the
+// epilogue warps add the chunks' sums up in registers with f32 adds. K-step kb of a tile is
+// step r = kb % (3 cs) of chunk q = kb / (3 cs): part p = r / cs (0: A_lo.B_hi, 1: A_hi.B_lo,
+// 2: A_hi.B_hi) at 32-wide column j = q cs + r % cs of K.
 struct Tf32x3Operands {
   using T = float;
   static constexpr int kStep = 32;
   static constexpr int kSegments = 3;
+  static constexpr bool kChunked = true;
   static constexpr uint32_t kFormat = 2;  // tf32 (kind::tf32)
   static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t per) {
-    const int64_t seg = kb / per, j = kb - seg * per;
-    return (int32_t)((seg == 2 ? per + j : j) * kStep);
+  // K-steps per chunk of each product, for `per` 32-wide steps in all
+  __host__ __device__ __forceinline__ static int64_t chunk_steps(int64_t per) {
+    int64_t cs = per < 8 ? per : 8;
+    while (per % cs != 0) --cs;
+    return cs;
   }
-  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t per) {
-    const int64_t seg = kb / per, j = kb - seg * per;
-    return (int32_t)((seg == 1 ? per + j : j) * kStep);
+  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t per, int64_t cs) {
+    const int64_t group = 3 * cs, q = kb / group, r = kb - q * group, p = r / cs;
+    const int64_t j = q * cs + (r - p * cs);
+    return (int32_t)((p == 0 ? per + j : j) * kStep);
+  }
+  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t per, int64_t cs) {
+    const int64_t group = 3 * cs, q = kb / group, r = kb - q * group, p = r / cs;
+    const int64_t j = q * cs + (r - p * cs);
+    return (int32_t)((p == 1 ? per + j : j) * kStep);
   }
 };
+
 
 // The instruction descriptor of an M x BN product with f32 accumulation for operands `Op`.
 template <class Op>
@@ -363,6 +381,41 @@ struct BiasQuads {
 };
 
 
+// The chunked form's epilogue pieces. A warp's share of a tile is 32 rows (its lane
+// quarter) x BN/2 columns (its half), held as sum[c][j] = column 32 c + j of the lane's row.
+__device__ __forceinline__ void add_chunk(float (&sum)[BN / 64][32], uint32_t acc, int half) {
+#pragma unroll
+  for (int c = 0; c < BN / 64; ++c) {
+    uint32_t r[32];
+    tmem_ld32(acc + (uint32_t)((half * (BN / 64) + c) * 32), r);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sum[c][j] += __uint_as_float(r[j]);
+  }
+}
+
+// Hand the summed share to the epilogue's store_column, one column of 32 rows per lane
+// (turned through the warp's staging rows, as epilogue_tile's column form).
+template <class Epi>
+__device__ __forceinline__ void store_sum(const Epi& epi, float (*stage_rows)[EPI_PITCH],
+                                          const float (&sum)[BN / 64][32], int half, int lane,
+                                          int64_t row0, int64_t col0, int64_t rows,
+                                          int64_t n) {
+#pragma unroll
+  for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stage_rows[lane][j] = sum[c][j];
+    __syncwarp();
+    const int64_t col = col0 + (half * (BN / 64) + c) * 32 + lane;
+    if (col < n && rows > 0) {
+      float column[32];
+#pragma unroll
+      for (int rr = 0; rr < 32; ++rr) column[rr] = stage_rows[rr][lane];
+      epi.store_column(column, row0, col, rows);
+    }
+    __syncwarp();
+  }
+}
+
 // One accumulator tile's epilogue for one warp: the 32 rows of its lane quarter (from row0,
 // `rows` of them inside C), the half of the BN columns from col0 + half * BN / 2; `acc` is the
 // TMEM address of the quarter's lanes at the accumulator's first column.
@@ -504,6 +557,12 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
   const int64_t m_blocks = (m + BM - 1) / BM, n_blocks = (n + BN - 1) / BN;
   const int64_t k_blocks = Op::kSegments * per;
   const int64_t tiles = m_blocks * n_blocks;
+  // K-steps that share one accumulator: the whole tile, or one chunk (Tf32x3Operands)
+  int64_t cs = 0, group = k_blocks;
+  if constexpr (Op::kChunked) {
+    cs = Op::chunk_steps(per);
+    group = 3 * cs;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -548,8 +607,9 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
             break;
           }
           mbar_expect_tx(&s.full[st], STAGE_BYTES);
-          tma_load_2d(s.stage[st], &map_a, &s.full[st], Op::a_col(kb, per), (int32_t)(mb * BM));
-          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], Op::b_col(kb, per),
+          tma_load_2d(s.stage[st], &map_a, &s.full[st], Op::a_col(kb, per, cs),
+                      (int32_t)(mb * BM));
+          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], Op::b_col(kb, per, cs),
                       (int32_t)(nb * BN));
         }
       }
@@ -560,16 +620,23 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---- MMA issuer
+      // ---- MMA issuer: one accumulator buffer per `group` K-steps (acc_it counts them)
       uint64_t it = 0, acc_it = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++acc_it) {
-        const int a = (int)(acc_it & 1);
-        const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
-        if (!mbar_wait(s, &s.acc_empty[a], aphase ^ 1, status)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(a * ACC_COLS);
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        uint32_t d = 0;
+        int64_t r = 0;  // K-step within the group
         for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int a = (int)(acc_it & 1);
+          if (r == 0) {
+            const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+            if (!mbar_wait(s, &s.acc_empty[a], aphase ^ 1, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d = tmem + (uint32_t)(a * ACC_COLS);
+          }
           const int st = (int)(it % STAGES);
           const uint32_t phase = (uint32_t)((it / STAGES) & 1);
           if (!mbar_wait(s, &s.full[st], phase, status)) {
@@ -583,11 +650,15 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             // advancing K by 32 bytes inside the swizzle row: +2 in addr >> 4
             mma_step<Op>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
-                         (kb > 0 || kk > 0) ? 1u : 0u);
+                         (r > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&s.empty[st]);
+          if (++r == group) {
+            mma_commit(&s.acc_full[a]);
+            ++acc_it;
+            r = 0;
+          }
         }
-        if (ok) mma_commit(&s.acc_full[a]);
       }
       // every MMA issued has finished before the accumulator memory is freed
       mma_commit(&s.drain);
@@ -601,22 +672,55 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
     const int half = ew >> 2;
     float(*stage_rows)[EPI_PITCH] = s.epi[ew];
     uint64_t acc_it = 0;
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_it) {
-      const int a = (int)(acc_it & 1);
-      const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
-      if (!mbar_wait(s, &s.acc_full[a], aphase, status)) break;
-      tc_fence_after();
-      int64_t mb, nb;
-      tile_coords(t, m_blocks, n_blocks, mb, nb);
-      const int64_t row0 = mb * BM + quarter * 32;
-      const int64_t col0 = nb * BN;
-      const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-      epilogue_tile(epi, stage_rows,
-                    tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
-                    lane, row0, col0, rows, n);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.acc_empty[a]);
+    if constexpr (Op::kChunked) {
+      // each chunk's accumulator added into registers, the tile stored after the last
+      const int64_t chunks = k_blocks / group;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        float sum[BN / 64][32];
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[c][j] = 0.f;
+        for (int64_t q = 0; q < chunks; ++q, ++acc_it) {
+          const int a = (int)(acc_it & 1);
+          const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+          if (!mbar_wait(s, &s.acc_full[a], aphase, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          add_chunk(sum, tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS),
+                    half);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.acc_empty[a]);
+        }
+        if (!ok) break;
+        int64_t mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        const int64_t row0 = mb * BM + quarter * 32;
+        const int64_t rows = m - row0 < 32 ? m - row0 : 32;
+        store_sum(epi, stage_rows, sum, half, lane, row0, nb * BN, rows, n);
+      }
+    } else {
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_it) {
+        const int a = (int)(acc_it & 1);
+        const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+        if (!mbar_wait(s, &s.acc_full[a], aphase, status)) break;
+        tc_fence_after();
+        int64_t mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        const int64_t row0 = mb * BM + quarter * 32;
+        const int64_t col0 = nb * BN;
+        const int64_t rows = m - row0 < 32 ? m - row0 : 32;
+        epilogue_tile(epi, stage_rows,
+                      tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
+                      lane, row0, col0, rows, n);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.acc_empty[a]);
+      }
     }
   }
   tc_fence_before();
@@ -754,6 +858,12 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
   const int64_t m_blocks = (m + 2 * BM - 1) / (2 * BM), n_blocks = (n + BN - 1) / BN;
   const int64_t per = k / Op::kStep;  // K-steps per operand segment
   const int64_t k_blocks = Op::kSegments * per, tiles = m_blocks * n_blocks;
+  // K-steps that share one accumulator: the whole tile, or one chunk (Tf32x3Operands)
+  int64_t cs = 0, group = k_blocks;
+  if constexpr (Op::kChunked) {
+    cs = Op::chunk_steps(per);
+    group = 3 * cs;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PAIR_STAGES; ++i) {
@@ -801,9 +911,9 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
           }
           if (first) mbar_expect_tx(&s.full[st], 2 * PAIR_STAGE_BYTES);
           const uint32_t bar = mapa_shared(smem_u32(&s.full[st]), 0);
-          tma_load_2d_pair(s.stage[st], &map_a, bar, Op::a_col(kb, per),
+          tma_load_2d_pair(s.stage[st], &map_a, bar, Op::a_col(kb, per, cs),
                            (int32_t)(mb * 2 * BM + rank * BM));
-          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, Op::b_col(kb, per),
+          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, Op::b_col(kb, per, cs),
                            (int32_t)(nb * BN + rank * (BN / 2)));
         }
       }
@@ -818,16 +928,23 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
   } else if (warp == 1) {
     if (lane == 0) {
       if (first) {
-        // ---- MMA issuer (first CTA)
+        // ---- MMA issuer (first CTA): one accumulator buffer per `group` K-steps
         uint64_t it = 0, acc_it = 0;
         bool ok = true;
-        for (int64_t t = pair; t < tiles && ok; t += pairs, ++acc_it) {
-          const int a = (int)(acc_it & 1);
-          const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
-          if (!mbar_wait(s, &s.acc_empty[a], aphase ^ 1, status)) break;
-          tc_fence_after();
-          const uint32_t d = tmem + (uint32_t)(a * ACC_COLS);
+        for (int64_t t = pair; t < tiles && ok; t += pairs) {
+          uint32_t d = 0;
+          int64_t r = 0;  // K-step within the group
           for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+            const int a = (int)(acc_it & 1);
+            if (r == 0) {
+              const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+              if (!mbar_wait(s, &s.acc_empty[a], aphase ^ 1, status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              d = tmem + (uint32_t)(a * ACC_COLS);
+            }
             const int st = (int)(it % PAIR_STAGES);
             const uint32_t phase = (uint32_t)((it / PAIR_STAGES) & 1);
             if (!mbar_wait(s, &s.full[st], phase, status)) {
@@ -840,10 +957,14 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
 #pragma unroll
             for (int kk = 0; kk < BK / UMMA_K; ++kk)
               mma_pair_step<Op>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
-                                (kb > 0 || kk > 0) ? 1u : 0u);
+                                (r > 0 || kk > 0) ? 1u : 0u);
             mma_commit_pair(&s.empty[st]);
+            if (++r == group) {
+              mma_commit_pair(&s.acc_full[a]);
+              ++acc_it;
+              r = 0;
+            }
           }
-          if (ok) mma_commit_pair(&s.acc_full[a]);
         }
         mma_commit_pair(&s.drain);
       }
@@ -857,22 +978,55 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
     const int half = ew >> 2;
     float(*stage_rows)[EPI_PITCH] = s.epi[ew];
     uint64_t acc_it = 0;
-    for (int64_t t = pair; t < tiles; t += pairs, ++acc_it) {
-      const int a = (int)(acc_it & 1);
-      const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
-      if (!mbar_wait(s, &s.acc_full[a], aphase, status)) break;
-      tc_fence_after();
-      int64_t mb, nb;
-      tile_coords(t, m_blocks, n_blocks, mb, nb);
-      const int64_t row0 = mb * 2 * BM + rank * BM + quarter * 32;
-      const int64_t col0 = nb * BN;
-      const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-      epilogue_tile(epi, stage_rows,
-                    tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
-                    lane, row0, col0, rows, n);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[a]), 0));
+    if constexpr (Op::kChunked) {
+      // each chunk's accumulator added into registers, the tile stored after the last
+      const int64_t chunks = k_blocks / group;
+      bool ok = true;
+      for (int64_t t = pair; t < tiles && ok; t += pairs) {
+        float sum[BN / 64][32];
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[c][j] = 0.f;
+        for (int64_t q = 0; q < chunks; ++q, ++acc_it) {
+          const int a = (int)(acc_it & 1);
+          const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+          if (!mbar_wait(s, &s.acc_full[a], aphase, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          add_chunk(sum, tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS),
+                    half);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[a]), 0));
+        }
+        if (!ok) break;
+        int64_t mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        const int64_t row0 = mb * 2 * BM + rank * BM + quarter * 32;
+        const int64_t rows = m - row0 < 32 ? m - row0 : 32;
+        store_sum(epi, stage_rows, sum, half, lane, row0, nb * BN, rows, n);
+      }
+    } else {
+      for (int64_t t = pair; t < tiles; t += pairs, ++acc_it) {
+        const int a = (int)(acc_it & 1);
+        const uint32_t aphase = (uint32_t)((acc_it >> 1) & 1);
+        if (!mbar_wait(s, &s.acc_full[a], aphase, status)) break;
+        tc_fence_after();
+        int64_t mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        const int64_t row0 = mb * 2 * BM + rank * BM + quarter * 32;
+        const int64_t col0 = nb * BN;
+        const int64_t rows = m - row0 < 32 ? m - row0 : 32;
+        epilogue_tile(epi, stage_rows,
+                      tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
+                      lane, row0, col0, rows, n);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[a]), 0));
+      }
     }
   }
   tc_fence_before();

@@ -22,7 +22,7 @@ REPO = HERE.parents[1]
 GOLDEN = REPO / "tests" / "golden"
 MODULES = ("gelu", "rows", "chain", "reductions", "collatz", "matmul", "matmul_bf16",
            "matmul_bf16_8192", "matmul_f32_4096", "gpt2_layernorm", "gelu_source", "views",
-           "collatz_threads")
+           "collatz_threads", "parallel_math")
 
 
 def regenerate(names=MODULES, compile_library: bool = False) -> list[Path]:

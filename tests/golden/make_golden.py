@@ -681,6 +681,120 @@ def _with_collatz_max(text: str) -> str:
     return encode(module)
 
 
+PARALLEL_MATH = '''
+import math
+
+from ppy import native, parallel
+
+
+def collatz_steps_of(n: int) -> int:
+    x = n
+    steps = 0
+    while x != 1:
+        if x % 2 == 0:
+            x = x // 2
+        else:
+            x = 3 * x + 1
+        steps += 1
+    return steps
+
+
+def math_table(out: native.ptr[float], lo: int, hi: int) -> int:
+    for i in parallel.range(lo, hi):
+        x = (i - 500) * 0.01
+        native.store(native.offset(out, i - lo), math.tanh(x) + math.erf(x) + math.atan2(x, 1.5))
+    return hi - lo
+
+
+def asin_table(out: native.ptr[float], lo: int, hi: int) -> int:
+    for i in parallel.range(lo, hi):
+        native.store(native.offset(out, i - lo), math.asin(i * 0.25))
+    return hi - lo
+'''
+
+
+def _with_collatz_map(text: str) -> str:
+    """Add @pmath_collatz_map(out, lo, hi): `parallel.map @pmath_collatz_steps_of() lo, hi,
+    out`, built with the reference's own builder (ir/dialects/parallel.py:184). The frontend
+    never emits parallel.map (a loop that stores per index becomes parallel.for), so the
+    op reaches a backend only from IR like this."""
+    from ppy_compiler.ir import I64, Builder, PtrType, decode, encode, verify
+    from ppy_compiler.ir.dialects import core, parallel
+
+    module = decode(text)
+    f = module.add_function("pmath_collatz_map",
+                            [("out", PtrType(I64)), ("lo", I64), ("hi", I64)], [I64])
+    f.attributes.update({"ppy.abi": "ppy", "ppy.symbol": "ppy_pmath_collatz_map",
+                         "ppy.qualname": "pmath.collatz_map"})
+    b = Builder(f.add_entry_block())
+    out, lo, hi = f.entry.arguments
+    parallel.map_(b, "pmath_collatz_steps_of", (), lo, hi, out)
+    core.ret(b, core.sub(b, hi, lo))
+    problems = verify(module)
+    assert not problems, problems
+    return encode(module)
+
+
+def _call_ptr(engine, symbol, out: np.ndarray, lo: int, hi: int) -> tuple[int, int]:
+    """Call a JIT'd function taking (ptr<T> out, i64 lo, i64 hi) and the result slot."""
+    slot = ctypes.c_int64(0)
+    fn = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                          ctypes.POINTER(ctypes.c_int64))(engine.address(symbol))
+    return int(fn(out.ctypes.data, lo, hi, ctypes.byref(slot))), int(slot.value)
+
+
+def golden_parallel_math(reference: Path) -> None:
+    """parallel.map, and parallel.for bodies that call the math externs: the IR as the
+    `openmp` route hands it to a backend (tests/golden/parallel_math.ppyir), and the outputs
+    of the reference's LLVM JIT of that IR (parallel_math.npz): the Collatz step counts of
+    [1, 5000) stored by the map at out[i], tanh(x) + erf(x) + atan2(x, 1.5) at x = (i -
+    500) / 100 for i in [0, 1000) through ppy_math_unary/binary (src/ppy_runtime/stdlib.c:
+    497-528), asin(i / 4) for i in [0, 5) (in its domain) and the status of [0, 8), where
+    asin(1.25) fails the domain guard around the call (lowering/stdlib.py:693-731)."""
+    from ppy_compiler.backend.llvm.from_ir import emit_module
+    from ppy_compiler.backend.llvm.ir_pipeline import optimize
+    from ppy_compiler.backend.llvm.jit import JitEngine
+    from ppy_compiler.driver.config import ParallelConfig
+    from ppy_compiler.ir import decode
+
+    with tempfile.TemporaryDirectory() as tmp:
+        root = Path(tmp)
+        (root / "pyproject.toml").write_text(
+            '[project]\nname = "pmath"\nversion = "0"\n\n[tool.ppy.parallel]\n'
+            'backend = "openmp"\n', encoding="utf-8")
+        (root / "pmath.ppy").write_text(textwrap.dedent(PARALLEL_MATH), encoding="utf-8")
+        text = _with_collatz_map(_ppy(reference, root, "emit", "ir", "pmath.ppy"))
+    (HERE / "parallel_math.ppyir").write_text(text, encoding="utf-8")
+    module = decode(text)
+    optimize(module, 2, parallel=ParallelConfig(backend="serial"))
+    engine = JitEngine(opt_level=2).open()
+    # ppy_math_unary/binary live in the reference's C runtime, which `ppy run` compiles into
+    # its cache and loads into the JIT (backend/llvm/__init__.py:1052-1069): the same here,
+    # with the cache in a temporary directory
+    with tempfile.TemporaryDirectory() as cache:
+        os.environ["XDG_CACHE_HOME"] = cache
+        from ppy_runtime.collections import library_path
+
+        runtime = library_path()
+        assert runtime is not None, "the reference's C runtime did not build"
+        engine.load_library(str(runtime))
+    engine.add(emit_module(module))
+    engine.finalize()
+    steps = np.full(5000, -1, np.int64)
+    map_status, map_value = _call_ptr(engine, "ppy_pmath_collatz_map", steps, 1, 5000)
+    table = np.zeros(1000, np.float64)
+    table_status, table_value = _call_ptr(engine, "ppy_pmath_math_table", table, 0, 1000)
+    asin_ok = np.zeros(5, np.float64)
+    asin_status, _ = _call_ptr(engine, "ppy_pmath_asin_table", asin_ok, 0, 5)
+    asin_bad = np.zeros(8, np.float64)
+    asin_bad_status, _ = _call_ptr(engine, "ppy_pmath_asin_table", asin_bad, 0, 8)
+    np.savez_compressed(
+        HERE / "parallel_math.npz", steps=steps, map_status=np.int32(map_status),
+        map_value=np.int64(map_value), table=table, table_status=np.int32(table_status),
+        table_value=np.int64(table_value), asin=asin_ok, asin_status=np.int32(asin_status),
+        asin_bad_status=np.int32(asin_bad_status))
+
+
 def golden_layernorm() -> None:
     """IR only: bf16 tensors are refused by the reference's LowerTensor; the parity of
     this module is checked against torch.layer_norm on the GPU."""
@@ -781,6 +895,7 @@ def main() -> None:
     golden_views()
     golden_collatz(options.reference)
     golden_collatz_threads(options.reference)
+    golden_parallel_math(options.reference)
     print("golden fixtures written to", HERE)
 
 

@@ -288,3 +288,55 @@ def test_a_body_that_never_ends_raises_instead_of_hanging(rt):
         module.collatz_collatz_sum(0, 1)
     g = json.loads((GOLDEN / "collatz.json").read_text())
     assert tuple(module.collatz_collatz_sum(1, 1000)) == (0, g["sum_1_1000"])
+
+
+# ---------------------------------------------------------------- parallel.map and math externs
+
+
+def _pmath(rt):
+    return rt.load(PREBUILT / "parallel_math" / "pmath.json")
+
+
+def test_parallel_map_stores_every_index_bit_exact(rt):
+    """`parallel.map @collatz_steps_of() lo, hi, out` (built with the reference's map_
+    builder, ir/dialects/parallel.py:184): out[i] = steps(i) for i in [1, 5000), out[0]
+    untouched, exactly the reference JIT's values and the oracle's."""
+    module = _pmath(rt)
+    d = np.load(GOLDEN / "parallel_math.npz")
+    out = torch.full((5000,), -1, dtype=torch.int64, device="cuda")
+    assert tuple(module.pmath_collatz_map(out, 1, 5000)) == (int(d["map_status"]),
+                                                            int(d["map_value"]))
+    assert np.array_equal(out.cpu().numpy(), d["steps"])
+    assert np.array_equal(out.cpu().numpy()[1:], oracle.collatz_steps(1, 5000)[1])
+    # a large range against the oracle, and an empty one that writes nothing
+    big = torch.zeros(1 << 20, dtype=torch.int64, device="cuda")
+    assert module.pmath_collatz_map(big, 1, 1 << 20).status == 0
+    assert np.array_equal(big.cpu().numpy()[1:], oracle.collatz_steps(1, 1 << 20)[1])
+    assert tuple(module.pmath_collatz_map(out, 7, 7)) == (0, 0)
+
+
+def test_math_externs_in_a_parallel_body(rt):
+    """tanh + erf + atan2 through ppy_math_unary/binary in a parallel.for body, against the
+    reference JIT's values (libm). CUDA's double tanh, erf and atan2 are within 2 ulp of the
+    correctly rounded result, so the sum of three is within a few ulp:
+    |y - ref| <= 1e-14 * max(|ref|, 1)."""
+    module = _pmath(rt)
+    d = np.load(GOLDEN / "parallel_math.npz")
+    out = torch.zeros(1000, dtype=torch.float64, device="cuda")
+    assert tuple(module.pmath_math_table(out, 0, 1000)) == (int(d["table_status"]),
+                                                           int(d["table_value"]))
+    within(out.cpu().numpy(), d["table"], rel=1e-14)
+    within(out.cpu().numpy(), oracle.math_table(0, 1000), rel=1e-14)
+
+
+def test_math_domain_guard_takes_the_fallback(rt):
+    """asin(i / 4): in its domain for i < 5 (values within 1e-14), and for [0, 8) asin(1.25)
+    fails the domain guard around the extern: FALLBACK, as the reference's JIT returns."""
+    module = _pmath(rt)
+    d = np.load(GOLDEN / "parallel_math.npz")
+    out = torch.zeros(8, dtype=torch.float64, device="cuda")
+    assert module.pmath_asin_table(out, 0, 5).status == int(d["asin_status"]) == 0
+    within(out[:5].cpu().numpy(), d["asin"], rel=1e-14)
+    assert module.pmath_asin_table(out, 0, 8).status == int(d["asin_bad_status"]) == 1
+    # the status word is per call: the next call is clean
+    assert module.pmath_asin_table(out, 0, 5).status == 0

@@ -114,3 +114,18 @@ def test_view_fixtures_follow_the_strided_views():
     at = oracle.transpose(d["matmul_t_in0"], (1, 0))
     assert np.allclose(d["matmul_t_out"], at.astype(np.float64) @ d["matmul_t_in1"], rtol=1e-5,
                        atol=1e-5)
+
+
+def test_parallel_math_oracle_is_bit_exact_with_the_reference():
+    """parallel.map and math-extern bodies (tests/golden/parallel_math.*, the reference's JIT
+    with its C runtime): Collatz steps stored by the map, tanh + erf + atan2 through
+    ppy_math_unary/binary, asin in its domain, and the domain guard's fallback."""
+    d = np.load(GOLDEN / "parallel_math.npz")
+    assert int(d["map_status"]) == 0 and int(d["map_value"]) == 4999
+    status, steps = oracle.collatz_steps(1, 5000)
+    assert status == 0 and np.array_equal(d["steps"][1:], steps) and d["steps"][0] == -1
+    assert int(d["table_status"]) == 0 and int(d["table_value"]) == 1000
+    assert np.array_equal(oracle.math_table(0, 1000), d["table"])
+    status, values = oracle.asin_table(0, 5)
+    assert status == int(d["asin_status"]) == 0 and np.array_equal(values, d["asin"])
+    assert oracle.asin_table(0, 8)[0] == int(d["asin_bad_status"]) == oracle.STATUS_FALLBACK
