@@ -270,6 +270,19 @@ int32_t ppyb200_tp_accumulate(float *x, const float *bias, const float *exchange
                               const int32_t *flags, int32_t ranks, int64_t m, int64_t n,
                               int32_t epoch, int32_t *status);
 
+/* ---------------------------------------------------------------- measurement */
+
+/* The issue ceiling of the Collatz step body of the parallel.range reduction (the reference's
+ * collatz_sum__par1 in tests/golden/collatz.ppyir: the x != 1 and parity tests, x / 2 or the
+ * checked 3x + 1, the checked step count, the trip bound): every lane of a full grid runs four
+ * independent chains of that step, branch-free, `steps_per_chain` steps each, so nothing
+ * diverges. `checksum` is a device int64 the kernel may add to (keeps the chains live);
+ * *total_steps (host) receives the steps the launch performs. No counterpart in the reference:
+ * the benchmark divides the reduction's steps/s by this kernel's to give its roofline fraction.
+ * Enqueued on the current stream. */
+int32_t ppyb200_collatz_step_peak(int64_t steps_per_chain, int64_t *checksum,
+                                  int64_t *total_steps);
+
 /* ---------------------------------------------------------------- without allocation */
 
 /* Floats in the fixed device array ppyb200_colmax_abs_f32_noalloc keeps its partials in. */

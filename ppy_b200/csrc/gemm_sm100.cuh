@@ -38,27 +38,20 @@ namespace ppyb200 {
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BN = 256;  // tile width; 192 where N is a multiple of 192 (pick_tile_n)
 constexpr int BK = 64;  // 64 bf16 = 128 bytes: one swizzle row
 constexpr int UMMA_K = 16;
 constexpr int STAGES = 4;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int ACC_COLS = BN;        // f32 accumulator columns per buffer
-constexpr int TMEM_COLS = 2 * ACC_COLS;
+// two accumulators of up to BN f32 columns (at columns 0 and TBN of the allocation)
+constexpr int TMEM_COLS = 2 * BN;
 constexpr int EPI_PITCH = 33;       // floats per staged row (32 + 1 pad: no bank conflicts)
 constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
 constexpr int GROUP_M = 16;         // tiles walk bands of 16 M-blocks for L2 reuse
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 
-// bf16 x bf16 -> f32, M = 128, N = 256, both operands K-major (PTX ISA, tcgen05
-// instruction descriptor: c_format bits 4-5, a/b format bits 7-12, N>>3 at bit 17,
-// M>>4 at bit 24).
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
 
 // What a kernel's operands are. Every K-step loads one 128-byte swizzle row of each operand
 // row (64 bf16 or 32 f32) and issues four MMAs of 32 bytes of K each (K = 16 bf16, or K = 8
@@ -124,16 +117,22 @@ struct Tf32x3Operands {
 };
 
 
-// The instruction descriptor of an M x BN product with f32 accumulation for operands `Op`.
-template <class Op>
+// The instruction descriptor of an M x TBN product with f32 accumulation for operands `Op`,
+// both K-major (PTX ISA, tcgen05 instruction descriptor: c_format bits 4-5, a/b format bits
+// 7-12, N>>3 at bit 17, M>>4 at bit 24).
+template <class Op, int TBN = BN>
 constexpr uint32_t idesc(int m) {
-  return (1u << 4) | (Op::kFormat << 7) | (Op::kFormat << 10) | ((uint32_t)(BN >> 3) << 17) |
+  return (1u << 4) | (Op::kFormat << 7) | (Op::kFormat << 10) | ((uint32_t)(TBN >> 3) << 17) |
          ((uint32_t)(m >> 4) << 24);
 }
 
-struct Shared {
+// The one-CTA kernel's shared memory for tiles TBN columns wide (256, or 192 for N a multiple
+// of 192: see pick_tile_n).
+template <int TBN>
+struct SharedT {
+  static constexpr int kStageBytes = A_BYTES + TBN * BK * 2;
   // the operand ring, 1024-byte aligned for the 128-byte swizzle
-  alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
+  alignas(1024) uint8_t stage[STAGES][kStageBytes];
   float epi[EPI_WARPS][32][EPI_PITCH];
   alignas(8) uint64_t full[STAGES];
   alignas(8) uint64_t empty[STAGES];
@@ -212,17 +211,8 @@ __device__ __forceinline__ uint64_t smem_desc(const void* tile) {
          (1ull << 46) | (2ull << 61);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate));
-}
-
-// One M=128 x N=256 MMA of 32 bytes of K from the operand tiles at adesc, bdesc.
-template <class Op>
+// One M=128 x N=TBN MMA of 32 bytes of K from the operand tiles at adesc, bdesc.
+template <class Op, int TBN>
 __device__ __forceinline__ void mma_step(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t accumulate) {
   if constexpr (Op::kFormat == 2) {
@@ -230,9 +220,13 @@ __device__ __forceinline__ void mma_step(uint32_t tmem_d, uint64_t adesc, uint64
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc<Op>(BM)), "r"(accumulate));
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op, TBN>(BM)), "r"(accumulate));
   } else {
-    mma_bf16(tmem_d, adesc, bdesc, accumulate);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op, TBN>(BM)), "r"(accumulate));
   }
 }
 
@@ -382,12 +376,13 @@ struct BiasQuads {
 
 
 // The chunked form's epilogue pieces. A warp's share of a tile is 32 rows (its lane
-// quarter) x BN/2 columns (its half), held as sum[c][j] = column 32 c + j of the lane's row.
-__device__ __forceinline__ void add_chunk(float (&sum)[BN / 64][32], uint32_t acc, int half) {
+// quarter) x TBN/2 columns (its half), held as sum[c][j] = column 32 c + j of the lane's row.
+template <int TBN>
+__device__ __forceinline__ void add_chunk(float (&sum)[TBN / 64][32], uint32_t acc, int half) {
 #pragma unroll
-  for (int c = 0; c < BN / 64; ++c) {
+  for (int c = 0; c < TBN / 64; ++c) {
     uint32_t r[32];
-    tmem_ld32(acc + (uint32_t)((half * (BN / 64) + c) * 32), r);
+    tmem_ld32(acc + (uint32_t)((half * (TBN / 64) + c) * 32), r);
 #pragma unroll
     for (int j = 0; j < 32; ++j) sum[c][j] += __uint_as_float(r[j]);
   }
@@ -395,17 +390,17 @@ __device__ __forceinline__ void add_chunk(float (&sum)[BN / 64][32], uint32_t ac
 
 // Hand the summed share to the epilogue's store_column, one column of 32 rows per lane
 // (turned through the warp's staging rows, as epilogue_tile's column form).
-template <class Epi>
+template <int TBN, class Epi>
 __device__ __forceinline__ void store_sum(const Epi& epi, float (*stage_rows)[EPI_PITCH],
-                                          const float (&sum)[BN / 64][32], int half, int lane,
+                                          const float (&sum)[TBN / 64][32], int half, int lane,
                                           int64_t row0, int64_t col0, int64_t rows,
                                           int64_t n) {
 #pragma unroll
-  for (int c = 0; c < BN / 64; ++c) {
+  for (int c = 0; c < TBN / 64; ++c) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) stage_rows[lane][j] = sum[c][j];
     __syncwarp();
-    const int64_t col = col0 + (half * (BN / 64) + c) * 32 + lane;
+    const int64_t col = col0 + (half * (TBN / 64) + c) * 32 + lane;
     if (col < n && rows > 0) {
       float column[32];
 #pragma unroll
@@ -417,18 +412,19 @@ __device__ __forceinline__ void store_sum(const Epi& epi, float (*stage_rows)[EP
 }
 
 // One accumulator tile's epilogue for one warp: the 32 rows of its lane quarter (from row0,
-// `rows` of them inside C), the half of the BN columns from col0 + half * BN / 2; `acc` is the
+// `rows` of them inside C), the half of the TBN columns from col0 + half * TBN / 2; `acc` is the
 // TMEM address of the quarter's lanes at the accumulator's first column.
-template <class Epi>
+template <int TBN, class Epi>
 __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows)[EPI_PITCH],
                                               uint32_t acc, int half, int lane, int64_t row0,
                                               int64_t col0, int64_t rows, int64_t n) {
   if constexpr (takes_lines<Epi>::value) {
+    static_assert(TBN % 128 == 0, "the lines form takes pairs of 32-column chunks per half");
     uint4* line = reinterpret_cast<uint4*>(&stage_rows[0][0]);  // 32 rows x 8 slots of 16 B
     const int slot = lane & 7;
 #pragma unroll 1
-    for (int c2 = 0; c2 < BN / 64; c2 += 2) {
-      const int chunk = half * (BN / 64) + c2;
+    for (int c2 = 0; c2 < TBN / 64; c2 += 2) {
+      const int chunk = half * (TBN / 64) + c2;
       const int64_t col = col0 + chunk * 32;  // the line's first column (N % 64 == 0: whole)
       if constexpr (has_is_line<Epi>::value) {
         if (!epi.is_line(col)) {  // the same for the whole warp: it depends on col alone
@@ -489,8 +485,8 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows
     return;
   }
 #pragma unroll 1
-  for (int c4 = 0; c4 < BN / 64; ++c4) {
-    const int chunk = half * (BN / 64) + c4;
+  for (int c4 = 0; c4 < TBN / 64; ++c4) {
+    const int chunk = half * (TBN / 64) + c4;
     uint32_t r[32];
     tmem_ld32(acc + (uint32_t)(chunk * 32), r);
     if constexpr (takes_rows<Epi>::value) {
@@ -543,18 +539,18 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows
 
 // The one-CTA kernel's body, for operands `Op`; `k` is the columns of one operand segment
 // (K for bf16, Kp for tf32x3), a multiple of Op::kStep.
-template <class Op, class Epi>
+template <class Op, int TBN, class Epi>
 __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
                                                    const CUtensorMap& map_b, int64_t m,
                                                    int64_t n, int64_t k, const Epi& epi,
                                                    int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
-  Shared& s = *reinterpret_cast<Shared*>(
+  SharedT<TBN>& s = *reinterpret_cast<SharedT<TBN>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t per = k / Op::kStep;  // K-steps per operand segment
-  const int64_t m_blocks = (m + BM - 1) / BM, n_blocks = (n + BN - 1) / BN;
+  const int64_t m_blocks = (m + BM - 1) / BM, n_blocks = (n + TBN - 1) / TBN;
   const int64_t k_blocks = Op::kSegments * per;
   const int64_t tiles = m_blocks * n_blocks;
   // K-steps that share one accumulator: the whole tile, or one chunk (Tf32x3Operands)
@@ -606,11 +602,11 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
             ok = false;
             break;
           }
-          mbar_expect_tx(&s.full[st], STAGE_BYTES);
+          mbar_expect_tx(&s.full[st], SharedT<TBN>::kStageBytes);
           tma_load_2d(s.stage[st], &map_a, &s.full[st], Op::a_col(kb, per, cs),
                       (int32_t)(mb * BM));
           tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], Op::b_col(kb, per, cs),
-                      (int32_t)(nb * BN));
+                      (int32_t)(nb * TBN));
         }
       }
       // the copies this thread issued land before the CTA may leave
@@ -635,7 +631,7 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
               break;
             }
             tc_fence_after();
-            d = tmem + (uint32_t)(a * ACC_COLS);
+            d = tmem + (uint32_t)(a * TBN);
           }
           const int st = (int)(it % STAGES);
           const uint32_t phase = (uint32_t)((it / STAGES) & 1);
@@ -649,7 +645,7 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             // advancing K by 32 bytes inside the swizzle row: +2 in addr >> 4
-            mma_step<Op>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
+            mma_step<Op, TBN>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
                          (r > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&s.empty[st]);
@@ -677,9 +673,9 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
       const int64_t chunks = k_blocks / group;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        float sum[BN / 64][32];
+        float sum[TBN / 64][32];
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c)
+        for (int c = 0; c < TBN / 64; ++c)
 #pragma unroll
           for (int j = 0; j < 32; ++j) sum[c][j] = 0.f;
         for (int64_t q = 0; q < chunks; ++q, ++acc_it) {
@@ -690,7 +686,7 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
             break;
           }
           tc_fence_after();
-          add_chunk(sum, tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS),
+          add_chunk<TBN>(sum, tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * TBN),
                     half);
           tc_fence_before();
           __syncwarp();
@@ -701,7 +697,7 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
         tile_coords(t, m_blocks, n_blocks, mb, nb);
         const int64_t row0 = mb * BM + quarter * 32;
         const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-        store_sum(epi, stage_rows, sum, half, lane, row0, nb * BN, rows, n);
+        store_sum<TBN>(epi, stage_rows, sum, half, lane, row0, nb * TBN, rows, n);
       }
     } else {
       for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_it) {
@@ -712,10 +708,10 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
         int64_t mb, nb;
         tile_coords(t, m_blocks, n_blocks, mb, nb);
         const int64_t row0 = mb * BM + quarter * 32;
-        const int64_t col0 = nb * BN;
+        const int64_t col0 = nb * TBN;
         const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-        epilogue_tile(epi, stage_rows,
-                      tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
+        epilogue_tile<TBN>(epi, stage_rows,
+                      tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * TBN), half,
                       lane, row0, col0, rows, n);
         tc_fence_before();
         __syncwarp();
@@ -732,20 +728,20 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
   }
 }
 
-template <class Epi>
+template <class Epi, int TBN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
                        int64_t k, Epi epi, int32_t* status) {
-  matmul_single_body<Bf16Operands>(map_a, map_b, m, n, k, epi, status);
+  matmul_single_body<Bf16Operands, TBN>(map_a, map_b, m, n, k, epi, status);
 }
 
-template <class Epi>
+template <class Epi, int TBN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a,
                          const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
                          int64_t k, Epi epi, int32_t* status) {
-  matmul_single_body<Tf32x3Operands>(map_a, map_b, m, n, k, epi, status);
+  matmul_single_body<Tf32x3Operands, TBN>(map_a, map_b, m, n, k, epi, status);
 }
 
 // ---- the 2-CTA form: a cluster of two CTAs on two SMs computes 256 x 256 tiles with
@@ -761,11 +757,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Every wait is bounded as in the one-CTA kernel; the two CTAs meet at cluster barriers only
 // before and after their loops, which every path leaves.
 constexpr int PAIR_STAGES = 5;
-constexpr int PAIR_B_BYTES = (BN / 2) * BK * 2;
-constexpr int PAIR_STAGE_BYTES = A_BYTES + PAIR_B_BYTES;
 
-struct PairShared {
-  alignas(1024) uint8_t stage[PAIR_STAGES][PAIR_STAGE_BYTES];
+template <int TBN>
+struct PairSharedT {
+  static constexpr int kStageBytes = A_BYTES + (TBN / 2) * BK * 2;  // each CTA's half of B
+  alignas(1024) uint8_t stage[PAIR_STAGES][kStageBytes];
   float epi[EPI_WARPS][32][EPI_PITCH];
   alignas(8) uint64_t full[PAIR_STAGES];
   alignas(8) uint64_t empty[PAIR_STAGES];
@@ -803,8 +799,8 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
-// One M=256 x N=256 MMA of 32 bytes of K over the pair (issued by the first CTA).
-template <class Op>
+// One M=256 x N=TBN MMA of 32 bytes of K over the pair (issued by the first CTA).
+template <class Op, int TBN>
 __device__ __forceinline__ void mma_pair_step(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                               uint32_t accumulate) {
   if constexpr (Op::kFormat == 2) {
@@ -812,13 +808,13 @@ __device__ __forceinline__ void mma_pair_step(uint32_t tmem_d, uint64_t adesc, u
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc<Op>(2 * BM)), "r"(accumulate));
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op, TBN>(2 * BM)), "r"(accumulate));
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc<Op>(2 * BM)), "r"(accumulate));
+        "l"(adesc), "l"(bdesc), "r"(idesc<Op, TBN>(2 * BM)), "r"(accumulate));
   }
 }
 
@@ -842,20 +838,20 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 }
 
 // The 2-CTA kernel's body, for operands `Op` (`k` as for matmul_single_body).
-template <class Op, class Epi>
+template <class Op, int TBN, class Epi>
 __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
                                                  const CUtensorMap& map_b, int64_t m,
                                                  int64_t n, int64_t k, const Epi& epi,
                                                  int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
-  PairShared& s = *reinterpret_cast<PairShared*>(
+  PairSharedT<TBN>& s = *reinterpret_cast<PairSharedT<TBN>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool first = rank == 0;
   const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
-  const int64_t m_blocks = (m + 2 * BM - 1) / (2 * BM), n_blocks = (n + BN - 1) / BN;
+  const int64_t m_blocks = (m + 2 * BM - 1) / (2 * BM), n_blocks = (n + TBN - 1) / TBN;
   const int64_t per = k / Op::kStep;  // K-steps per operand segment
   const int64_t k_blocks = Op::kSegments * per, tiles = m_blocks * n_blocks;
   // K-steps that share one accumulator: the whole tile, or one chunk (Tf32x3Operands)
@@ -909,12 +905,12 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
             ok = false;
             break;
           }
-          if (first) mbar_expect_tx(&s.full[st], 2 * PAIR_STAGE_BYTES);
+          if (first) mbar_expect_tx(&s.full[st], 2 * PairSharedT<TBN>::kStageBytes);
           const uint32_t bar = mapa_shared(smem_u32(&s.full[st]), 0);
           tma_load_2d_pair(s.stage[st], &map_a, bar, Op::a_col(kb, per, cs),
                            (int32_t)(mb * 2 * BM + rank * BM));
           tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, Op::b_col(kb, per, cs),
-                           (int32_t)(nb * BN + rank * (BN / 2)));
+                           (int32_t)(nb * TBN + rank * (TBN / 2)));
         }
       }
       // the pair's copies land before the CTAs may leave (they all complete on the first
@@ -943,7 +939,7 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
                 break;
               }
               tc_fence_after();
-              d = tmem + (uint32_t)(a * ACC_COLS);
+              d = tmem + (uint32_t)(a * TBN);
             }
             const int st = (int)(it % PAIR_STAGES);
             const uint32_t phase = (uint32_t)((it / PAIR_STAGES) & 1);
@@ -956,7 +952,7 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
             const uint64_t bdesc = smem_desc(s.stage[st] + A_BYTES);
 #pragma unroll
             for (int kk = 0; kk < BK / UMMA_K; ++kk)
-              mma_pair_step<Op>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
+              mma_pair_step<Op, TBN>(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2),
                                 (r > 0 || kk > 0) ? 1u : 0u);
             mma_commit_pair(&s.empty[st]);
             if (++r == group) {
@@ -983,9 +979,9 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
       const int64_t chunks = k_blocks / group;
       bool ok = true;
       for (int64_t t = pair; t < tiles && ok; t += pairs) {
-        float sum[BN / 64][32];
+        float sum[TBN / 64][32];
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c)
+        for (int c = 0; c < TBN / 64; ++c)
 #pragma unroll
           for (int j = 0; j < 32; ++j) sum[c][j] = 0.f;
         for (int64_t q = 0; q < chunks; ++q, ++acc_it) {
@@ -996,7 +992,7 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
             break;
           }
           tc_fence_after();
-          add_chunk(sum, tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS),
+          add_chunk<TBN>(sum, tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * TBN),
                     half);
           tc_fence_before();
           __syncwarp();
@@ -1007,7 +1003,7 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
         tile_coords(t, m_blocks, n_blocks, mb, nb);
         const int64_t row0 = mb * 2 * BM + rank * BM + quarter * 32;
         const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-        store_sum(epi, stage_rows, sum, half, lane, row0, nb * BN, rows, n);
+        store_sum<TBN>(epi, stage_rows, sum, half, lane, row0, nb * TBN, rows, n);
       }
     } else {
       for (int64_t t = pair; t < tiles; t += pairs, ++acc_it) {
@@ -1018,10 +1014,10 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
         int64_t mb, nb;
         tile_coords(t, m_blocks, n_blocks, mb, nb);
         const int64_t row0 = mb * 2 * BM + rank * BM + quarter * 32;
-        const int64_t col0 = nb * BN;
+        const int64_t col0 = nb * TBN;
         const int64_t rows = m - row0 < 32 ? m - row0 : 32;
-        epilogue_tile(epi, stage_rows,
-                      tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC_COLS), half,
+        epilogue_tile<TBN>(epi, stage_rows,
+                      tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * TBN), half,
                       lane, row0, col0, rows, n);
         tc_fence_before();
         __syncwarp();
@@ -1039,20 +1035,20 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
   }
 }
 
-template <class Epi>
+template <class Epi, int TBN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                             const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
                             int64_t k, Epi epi, int32_t* status) {
-  matmul_pair_body<Bf16Operands>(map_a, map_b, m, n, k, epi, status);
+  matmul_pair_body<Bf16Operands, TBN>(map_a, map_b, m, n, k, epi, status);
 }
 
-template <class Epi>
+template <class Epi, int TBN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                               const __grid_constant__ CUtensorMap map_b, int64_t m, int64_t n,
                               int64_t k, Epi epi, int32_t* status) {
-  matmul_pair_body<Tf32x3Operands>(map_a, map_b, m, n, k, epi, status);
+  matmul_pair_body<Tf32x3Operands, TBN>(map_a, map_b, m, n, k, epi, status);
 }
 
 // ---- host side
@@ -1104,51 +1100,53 @@ inline bool tileable(int64_t m, int64_t n, int64_t k) {
          n < (1ll << 31);
 }
 
-inline size_t shared_bytes() { return sizeof(Shared) + 1024; }
+template <int TBN = BN>
+inline size_t shared_bytes() { return sizeof(SharedT<TBN>) + 1024; }
 
-// The __global__ kernels of operands `Op` with epilogue `Epi`.
-template <class Op, class Epi>
+// The __global__ kernels of operands `Op` with epilogue `Epi`, tiles TBN columns wide.
+template <class Op, class Epi, int TBN>
 struct Kernels;
-template <class Epi>
-struct Kernels<Bf16Operands, Epi> {
-  static constexpr auto single = matmul_bf16_kernel<Epi>;
-  static constexpr auto pair = matmul_bf16_pair_kernel<Epi>;
+template <class Epi, int TBN>
+struct Kernels<Bf16Operands, Epi, TBN> {
+  static constexpr auto single = matmul_bf16_kernel<Epi, TBN>;
+  static constexpr auto pair = matmul_bf16_pair_kernel<Epi, TBN>;
 };
-template <class Epi>
-struct Kernels<Tf32x3Operands, Epi> {
-  static constexpr auto single = matmul_tf32x3_kernel<Epi>;
-  static constexpr auto pair = matmul_tf32x3_pair_kernel<Epi>;
+template <class Epi, int TBN>
+struct Kernels<Tf32x3Operands, Epi, TBN> {
+  static constexpr auto single = matmul_tf32x3_kernel<Epi, TBN>;
+  static constexpr auto pair = matmul_tf32x3_pair_kernel<Epi, TBN>;
 };
 
 // The one-CTA kernel on `stream` over operand matrices a [m, Op::kSegments > 1 ? 2k : k] and
 // bt [n, same] (see the operand structs); returns a cudaError_t (cudaErrorInvalidValue when
 // the maps cannot be made). The caller checks the shapes and 16-byte alignment of a, bt.
-template <class Op, class Epi>
+template <class Op, int TBN = BN, class Epi>
 inline cudaError_t launch_single_op(const typename Op::T* a, const typename Op::T* bt, int64_t m,
                                     int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
                                     cudaStream_t stream) {
   const int64_t cols = Op::kSegments > 1 ? 2 * k : k;
   CUtensorMap map_a, map_b;
-  if (!make_map<Op>(&map_a, a, m, cols, BM) || !make_map<Op>(&map_b, bt, n, cols, BN))
+  if (!make_map<Op>(&map_a, a, m, cols, BM) || !make_map<Op>(&map_b, bt, n, cols, TBN))
     return cudaErrorInvalidValue;
   static DeviceOnce configured;
   int ready = 0;
   cudaError_t e = configured.get(
       [](int* v) {
         *v = 1;
-        return cudaFuncSetAttribute(Kernels<Op, Epi>::single,
+        return cudaFuncSetAttribute(Kernels<Op, Epi, TBN>::single,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)shared_bytes());
+                                    (int)shared_bytes<TBN>());
       },
       &ready);
   if (e != cudaSuccess) return e;
-  const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int64_t tiles = ((m + BM - 1) / BM) * ((n + TBN - 1) / TBN);
   const int grid = (int)(tiles < sm_count ? tiles : sm_count);
-  return launch_pdl(Kernels<Op, Epi>::single, dim3(grid), dim3(THREADS), shared_bytes(), stream,
-                    map_a, map_b, m, n, k, epi, status);
+  return launch_pdl(Kernels<Op, Epi, TBN>::single, dim3(grid), dim3(THREADS),
+                    shared_bytes<TBN>(), stream, map_a, map_b, m, n, k, epi, status);
 }
 
-inline size_t pair_shared_bytes() { return sizeof(PairShared) + 1024; }
+template <int TBN = BN>
+inline size_t pair_shared_bytes() { return sizeof(PairSharedT<TBN>) + 1024; }
 
 // K from which a tile's MMAs, not its stores, set its pace (C = A.B + bias keeps the column
 // form there: quads measured 2.5 % slower at 8192^3, and faster at K = 768).
@@ -1157,13 +1155,13 @@ constexpr int64_t DEEP_K = 2048;
 
 // The 2-CTA kernel on `stream`: clusters of two CTAs, as many as can be resident at once (at
 // most one per 256 x 256 tile). Same contract as `launch_single_op`.
-template <class Op, class Epi>
+template <class Op, int TBN = BN, class Epi>
 inline cudaError_t launch_pair_op(const typename Op::T* a, const typename Op::T* bt, int64_t m,
                                   int64_t n, int64_t k, Epi epi, int32_t* status,
                                   cudaStream_t stream) {
   const int64_t cols = Op::kSegments > 1 ? 2 * k : k;
   CUtensorMap map_a, map_b;
-  if (!make_map<Op>(&map_a, a, m, cols, BM) || !make_map<Op>(&map_b, bt, n, cols, BN / 2))
+  if (!make_map<Op>(&map_a, a, m, cols, BM) || !make_map<Op>(&map_b, bt, n, cols, TBN / 2))
     return cudaErrorInvalidValue;
   static DeviceOnce resident;
   cudaLaunchConfig_t config = {};
@@ -1175,7 +1173,7 @@ inline cudaError_t launch_pair_op(const typename Op::T* a, const typename Op::T*
   attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attribute[1].val.programmaticStreamSerializationAllowed = 1;
   config.blockDim = dim3(THREADS, 1, 1);
-  config.dynamicSmemBytes = pair_shared_bytes();
+  config.dynamicSmemBytes = pair_shared_bytes<TBN>();
   config.stream = stream;
   config.attrs = attribute;
   config.numAttrs = 1;
@@ -1184,21 +1182,22 @@ inline cudaError_t launch_pair_op(const typename Op::T* a, const typename Op::T*
   int max_clusters = 0;
   cudaError_t e = resident.get(
       [&config](int* v) {
-        cudaError_t r = cudaFuncSetAttribute(Kernels<Op, Epi>::pair,
+        cudaError_t r = cudaFuncSetAttribute(Kernels<Op, Epi, TBN>::pair,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)pair_shared_bytes());
+                                             (int)pair_shared_bytes<TBN>());
         if (r != cudaSuccess) return r;
         cudaLaunchConfig_t probe = config;
         probe.gridDim = dim3(2, 1, 1);
-        return cudaOccupancyMaxActiveClusters(v, Kernels<Op, Epi>::pair, &probe);
+        return cudaOccupancyMaxActiveClusters(v, Kernels<Op, Epi, TBN>::pair, &probe);
       },
       &max_clusters);
   if (e != cudaSuccess) return e;
-  const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
+  const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + TBN - 1) / TBN);
   const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
   config.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
   config.numAttrs = ppyb200_pdl() ? 2 : 1;
-  return cudaLaunchKernelEx(&config, Kernels<Op, Epi>::pair, map_a, map_b, m, n, k, epi, status);
+  return cudaLaunchKernelEx(&config, Kernels<Op, Epi, TBN>::pair, map_a, map_b, m, n, k, epi,
+                            status);
 }
 
 template <class Epi>
@@ -1206,6 +1205,20 @@ inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt
                                  int64_t n, int64_t k, Epi epi, int32_t* status, int sm_count,
                                  cudaStream_t stream) {
   return launch_single_op<Bf16Operands>(a, bt, m, n, k, epi, status, sm_count, stream);
+}
+
+// The tile width for an m x n product on `units` SMs (one CTA per tile) or CTA pairs, in
+// rows of `block_rows`: 192 when n is a whole number of 192-wide tiles and fewer waves x
+// width are needed than with 256 -- GPT-2's N = 768 layers: at 32768 rows on CTA pairs 7
+// waves of 192 against 6 of 256 (384 tiles for 74 pairs), at 4096 rows 64 tiles of 192 in
+// one wave against 48 of 256 that leave 26 pairs idle -- else 256.
+inline int pick_tile_n(int64_t m, int64_t n, int64_t block_rows, int64_t units) {
+  if (n % 192 != 0 || units < 1) return BN;
+  const int64_t rows = (m + block_rows - 1) / block_rows;
+  const int64_t wide = rows * ((n + 255) / 256), narrow = rows * (n / 192);
+  const int64_t cost_wide = (wide + units - 1) / units * 256;
+  const int64_t cost_narrow = (narrow + units - 1) / units * 192;
+  return cost_narrow < cost_wide ? 192 : BN;
 }
 
 // The tensor-core GEMM: CTA pairs or one CTA per tile, as ppyb200_gemm_form() says (by shape
@@ -1220,8 +1233,17 @@ inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64
   // GPT-2 shape (32768 rows, K = 768: out projection 0.765 against 0.829 ms, QKV 1.32 against
   // 1.35, FC 1.92 against 1.95 per forward; K = 3072 and 8192: 3 % and 2.4 %). Below 256
   // rows half of each pair would idle.
-  if (form == PPYB200_GEMM_PAIRS || (form == PPYB200_GEMM_BY_SHAPE && m >= 2 * BM))
-    return launch_pair_op<Bf16Operands>(a, bt, m, n, k, epi, status, stream);
+  const bool pairs = form == PPYB200_GEMM_PAIRS || (form == PPYB200_GEMM_BY_SHAPE && m >= 2 * BM);
+  // the 192-wide tile for the epilogue forms that take it (not whole 128-byte lines of
+  // pairs of 32-column chunks); ppyb200_gemm_form pins 256 with its PAIRS / SINGLE values
+  if constexpr (!takes_lines<Epi>::value) {
+    if (form == PPYB200_GEMM_BY_SHAPE &&
+        pick_tile_n(m, n, pairs ? 2 * BM : BM, pairs ? sm_count / 2 : sm_count) == 192) {
+      if (pairs) return launch_pair_op<Bf16Operands, 192>(a, bt, m, n, k, epi, status, stream);
+      return launch_single_op<Bf16Operands, 192>(a, bt, m, n, k, epi, status, sm_count, stream);
+    }
+  }
+  if (pairs) return launch_pair_op<Bf16Operands>(a, bt, m, n, k, epi, status, stream);
   return launch_single_op<Bf16Operands>(a, bt, m, n, k, epi, status, sm_count, stream);
 }
 

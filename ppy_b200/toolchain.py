@@ -17,7 +17,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 INCLUDE = PACKAGE.parent / "include"
 RUNTIME_SOURCES = ("ppyb200_runtime.cu", "gemm_sm100.cu", "gpt2.cu", "noalloc.cu",
-                   "tp_exchange.cu")
+                   "tp_exchange.cu", "probes.cu")
 RUNTIME_LIBRARY = PACKAGE / "libppyb200.so"
 ARCH = "sm_100a"
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]

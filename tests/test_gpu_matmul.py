@@ -371,3 +371,33 @@ def test_f32_matmul_non_finite_inputs_follow_ieee(lib):
     scale = ref[finite].pow(2).mean().sqrt()
     assert float(((c[finite].double() - ref[finite]).abs() / torch.maximum(
         ref[finite].abs(), scale)).max()) <= 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 768, 768), (32768, 768, 3072), (300, 1152, 128),
+                                   (100, 768, 64)])
+def test_192_wide_tiles_match_256_wide_bit_for_bit(lib, m, n, k):
+    """N a multiple of 192: the default form takes 192-wide tiles where they need fewer
+    waves (pick_tile_n); every output element still sums its K products in the same order,
+    so the result equals the 256-wide tiles' (forms pinned by ppyb200_set_gemm_form) exactly,
+    for the column and the four-column-quads epilogues."""
+    a, b, bias = _operands(m, n, k, seed=11)
+    da, dbt, dbias = a.cuda(), b.t().contiguous().cuda(), bias.cuda()
+    ref = None
+    for ldc in (n, n + 4):  # quads (rows on 16-byte boundaries) at K < 2048, columns beyond
+        outs = {}
+        for form in (0, 1, 2):
+            out = torch.full((m, ldc), 5.0, device="cuda")
+            before = lib.ppyb200_set_gemm_form(form)
+            try:
+                assert lib.ppyb200_matmul_bf16_kmajor_ld(_ptr(da), _ptr(dbt), _ptr(dbias),
+                                                         _ptr(out), ldc, m, n, k) == 0
+            finally:
+                lib.ppyb200_set_gemm_form(before)
+            torch.cuda.synchronize()
+            outs[form] = out
+        pinned = outs[1] if m >= 256 else outs[2]
+        assert torch.equal(outs[0], pinned)
+        assert torch.all(outs[0][:, n:] == 5.0)
+        if ref is None:
+            ref = _reference(a[:512], b, bias)
+        _check(outs[0][:512, :n], ref, rel=1e-4)
