@@ -67,12 +67,15 @@ struct Bf16Operands {
   static constexpr bool kChunked = false;  // one accumulation per tile, over all of K
   static constexpr uint32_t kFormat = 1;  // bf16 (kind::f16)
   static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t, int64_t) {
-    return (int32_t)(kb * kStep);
-  }
-  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t, int64_t) {
-    return (int32_t)(kb * kStep);
-  }
+  // The columns of A and Bt the K-steps of a tile read, in order: kb * 64 for both.
+  struct Walk {
+    int64_t kb = 0;
+    __device__ __forceinline__ Walk(int64_t, int64_t) {}
+    __device__ __forceinline__ void restart() { kb = 0; }
+    __device__ __forceinline__ int32_t a_col() const { return (int32_t)(kb * kStep); }
+    __device__ __forceinline__ int32_t b_col() const { return (int32_t)(kb * kStep); }
+    __device__ __forceinline__ void next() { ++kb; }
+  };
 };
 
 // Tf32x3Operands: an f32 product A.B computed as three tf32 products on the tensor cores,
@@ -90,7 +93,7 @@ struct Bf16Operands {
 // into a fresh accumulator -- the small products first, while the sum is small -- and the
 // epilogue warps add the chunks' sums up in registers with f32 adds. K-step kb of a tile is
 // step r = kb % (3 cs) of chunk q = kb / (3 cs): part p = r / cs (0: A_lo.B_hi, 1: A_hi.B_lo,
-// 2: A_hi.B_hi) at 32-wide column j = q cs + r % cs of K.
+// 2: A_hi.B_hi) at 32-wide column j = q cs + r % cs of K (Walk keeps these as counters).
 struct Tf32x3Operands {
   using T = float;
   static constexpr int kStep = 32;
@@ -104,16 +107,35 @@ struct Tf32x3Operands {
     while (per % cs != 0) --cs;
     return cs;
   }
-  __device__ __forceinline__ static int32_t a_col(int64_t kb, int64_t per, int64_t cs) {
-    const int64_t group = 3 * cs, q = kb / group, r = kb - q * group, p = r / cs;
-    const int64_t j = q * cs + (r - p * cs);
-    return (int32_t)((p == 0 ? per + j : j) * kStep);
-  }
-  __device__ __forceinline__ static int32_t b_col(int64_t kb, int64_t per, int64_t cs) {
-    const int64_t group = 3 * cs, q = kb / group, r = kb - q * group, p = r / cs;
-    const int64_t j = q * cs + (r - p * cs);
-    return (int32_t)((p == 1 ? per + j : j) * kStep);
-  }
+  // The columns of A2 and B2t the K-steps of a tile read, in order, kept as counters
+  // (chunk q, part p, step jj within the part) so that a step costs no division.
+  struct Walk {
+    int64_t per, cs, q = 0, jj = 0;
+    int p = 0;
+    __device__ __forceinline__ Walk(int64_t per_, int64_t cs_) : per(per_), cs(cs_) {}
+    __device__ __forceinline__ void restart() {
+      q = 0;
+      jj = 0;
+      p = 0;
+    }
+    __device__ __forceinline__ int32_t a_col() const {
+      const int64_t j = q * cs + jj;
+      return (int32_t)((p == 0 ? per + j : j) * kStep);
+    }
+    __device__ __forceinline__ int32_t b_col() const {
+      const int64_t j = q * cs + jj;
+      return (int32_t)((p == 1 ? per + j : j) * kStep);
+    }
+    __device__ __forceinline__ void next() {
+      if (++jj == cs) {
+        jj = 0;
+        if (++p == 3) {
+          p = 0;
+          ++q;
+        }
+      }
+    }
+  };
 };
 
 
@@ -592,10 +614,12 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
       // ---- loader
       uint64_t it = 0;
       bool ok = true;
+      typename Op::Walk walk(per, cs);
       for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int64_t mb, nb;
         tile_coords(t, m_blocks, n_blocks, mb, nb);
-        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+        walk.restart();
+        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it, walk.next()) {
           const int st = (int)(it % STAGES);
           const uint32_t phase = (uint32_t)((it / STAGES) & 1);
           if (!mbar_wait(s, &s.empty[st], phase ^ 1, status)) {
@@ -603,9 +627,8 @@ __device__ __forceinline__ void matmul_single_body(const CUtensorMap& map_a,
             break;
           }
           mbar_expect_tx(&s.full[st], SharedT<TBN>::kStageBytes);
-          tma_load_2d(s.stage[st], &map_a, &s.full[st], Op::a_col(kb, per, cs),
-                      (int32_t)(mb * BM));
-          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], Op::b_col(kb, per, cs),
+          tma_load_2d(s.stage[st], &map_a, &s.full[st], walk.a_col(), (int32_t)(mb * BM));
+          tma_load_2d(s.stage[st] + A_BYTES, &map_b, &s.full[st], walk.b_col(),
                       (int32_t)(nb * TBN));
         }
       }
@@ -895,10 +918,12 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
       // ---- loader (both CTAs): this CTA's 128 rows of A and of B^T
       uint64_t it = 0;
       bool ok = true;
+      typename Op::Walk walk(per, cs);
       for (int64_t t = pair; t < tiles && ok; t += pairs) {
         int64_t mb, nb;
         tile_coords(t, m_blocks, n_blocks, mb, nb);
-        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it) {
+        walk.restart();
+        for (int64_t kb = 0; kb < k_blocks; ++kb, ++it, walk.next()) {
           const int st = (int)(it % PAIR_STAGES);
           const uint32_t phase = (uint32_t)((it / PAIR_STAGES) & 1);
           if (!mbar_wait(s, &s.empty[st], phase ^ 1, status)) {
@@ -907,9 +932,9 @@ __device__ __forceinline__ void matmul_pair_body(const CUtensorMap& map_a,
           }
           if (first) mbar_expect_tx(&s.full[st], 2 * PairSharedT<TBN>::kStageBytes);
           const uint32_t bar = mapa_shared(smem_u32(&s.full[st]), 0);
-          tma_load_2d_pair(s.stage[st], &map_a, bar, Op::a_col(kb, per, cs),
+          tma_load_2d_pair(s.stage[st], &map_a, bar, walk.a_col(),
                            (int32_t)(mb * 2 * BM + rank * BM));
-          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, Op::b_col(kb, per, cs),
+          tma_load_2d_pair(s.stage[st] + A_BYTES, &map_b, bar, walk.b_col(),
                            (int32_t)(nb * TBN + rank * (TBN / 2)));
         }
       }
@@ -1207,13 +1232,15 @@ inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt
   return launch_single_op<Bf16Operands>(a, bt, m, n, k, epi, status, sm_count, stream);
 }
 
-// The tile width for an m x n product on `units` SMs (one CTA per tile) or CTA pairs, in
-// rows of `block_rows`: 192 when n is a whole number of 192-wide tiles and fewer waves x
-// width are needed than with 256 -- GPT-2's N = 768 layers: at 32768 rows on CTA pairs 7
-// waves of 192 against 6 of 256 (384 tiles for 74 pairs), at 4096 rows 64 tiles of 192 in
-// one wave against 48 of 256 that leave 26 pairs idle -- else 256.
-inline int pick_tile_n(int64_t m, int64_t n, int64_t block_rows, int64_t units) {
-  if (n % 192 != 0 || units < 1) return BN;
+// The tile width for an m x n x k product on `units` SMs (one CTA per tile) or CTA pairs, in
+// rows of `block_rows`: 192 when K is shallow, n is a whole number of 192-wide tiles and
+// fewer waves x width are needed than with 256 -- GPT-2's out projection (N = 768, K = 768):
+// 0.744 against 0.793 ms per forward at 32768 rows (7 waves of 192 against 6 of 256 on 74
+// CTA pairs). At deep K a 192-wide tile loads a third more operand bytes per MMA than a
+// 256-wide one and the loads set the pace: the proj layer (K = 3072) took 2.09 against 1.79
+// ms. Else 256.
+inline int pick_tile_n(int64_t m, int64_t n, int64_t k, int64_t block_rows, int64_t units) {
+  if (k >= DEEP_K || n % 192 != 0 || units < 1) return BN;
   const int64_t rows = (m + block_rows - 1) / block_rows;
   const int64_t wide = rows * ((n + 255) / 256), narrow = rows * (n / 192);
   const int64_t cost_wide = (wide + units - 1) / units * 256;
@@ -1238,7 +1265,7 @@ inline cudaError_t launch(const __nv_bfloat16* a, const __nv_bfloat16* bt, int64
   // pairs of 32-column chunks); ppyb200_gemm_form pins 256 with its PAIRS / SINGLE values
   if constexpr (!takes_lines<Epi>::value) {
     if (form == PPYB200_GEMM_BY_SHAPE &&
-        pick_tile_n(m, n, pairs ? 2 * BM : BM, pairs ? sm_count / 2 : sm_count) == 192) {
+        pick_tile_n(m, n, k, pairs ? 2 * BM : BM, pairs ? sm_count / 2 : sm_count) == 192) {
       if (pairs) return launch_pair_op<Bf16Operands, 192>(a, bt, m, n, k, epi, status, stream);
       return launch_single_op<Bf16Operands, 192>(a, bt, m, n, k, epi, status, sm_count, stream);
     }

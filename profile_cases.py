@@ -6,6 +6,8 @@ one launch of it alone.
     python profile_cases.py attention   # causal_kernel, batch 32 x 1024, 12 heads
     python profile_cases.py fc          # matmul_bf16_pair_kernel, GELU epilogue,
                                                  # GPT-2 FC (32768 x 3072 x 768)
+    python profile_cases.py gemm_f32    # matmul_tf32x3_pair_kernel, f32 4096^3 (after the
+                                         # two split kernels of each call)
     python profile_cases.py lm_head     # matmul_bf16_pair_kernel, quads epilogue,
                                                  # 50257 logits a row in rows 50272 apart
 
@@ -29,7 +31,7 @@ def main() -> None:
     from ppy_b200 import gpt2, runtime
 
     parser = argparse.ArgumentParser()
-    parser.add_argument("case", choices=["gemm", "attention", "fc", "lm_head"])
+    parser.add_argument("case", choices=["gemm", "gemm_f32", "attention", "fc", "lm_head"])
     case = parser.parse_args().case
     runtime.init(0)
     stream = torch.cuda.Stream()
@@ -52,6 +54,16 @@ def main() -> None:
             a, bt, c, ldc, m, n, k = main.operands
             status = lib.ppyb200_matmul_bf16_kmajor_ld(a.data_ptr(), bt.data_ptr(), None,
                                                        c.data_ptr(), ldc, m, n, k)
+        elif case == "gemm_f32":
+            if not hasattr(main, "operands"):
+                import ctypes
+
+                lib.ppyb200_matmul_f32.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+                main.operands = tuple(rand(4096, 4096, dtype=torch.float32) for _ in range(2)) + (
+                    torch.empty(4096, 4096, device="cuda"),)
+            a, b, c = main.operands
+            status = lib.ppyb200_matmul_f32(a.data_ptr(), b.data_ptr(), None, c.data_ptr(),
+                                            4096, 4096, 4096)
         elif case == "attention":
             if not hasattr(main, "operands"):
                 main.operands = (rand(32 * 1024, 3 * 768), rand(32 * 12 * 64, 1024),

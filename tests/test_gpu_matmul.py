@@ -373,11 +373,12 @@ def test_f32_matmul_non_finite_inputs_follow_ieee(lib):
         ref[finite].abs(), scale)).max()) <= 1e-5
 
 
-@pytest.mark.parametrize("m,n,k", [(4096, 768, 768), (32768, 768, 3072), (300, 1152, 128),
-                                   (100, 768, 64)])
+@pytest.mark.parametrize("m,n,k", [(4096, 768, 768), (32768, 768, 1536), (300, 1152, 128),
+                                   (100, 768, 64), (4096, 768, 3072)])
 def test_192_wide_tiles_match_256_wide_bit_for_bit(lib, m, n, k):
     """N a multiple of 192: the default form takes 192-wide tiles where they need fewer
-    waves (pick_tile_n); every output element still sums its K products in the same order,
+    waves at shallow K (pick_tile_n; K = 3072 keeps 256); every output element still sums
+    its K products in the same order,
     so the result equals the 256-wide tiles' (forms pinned by ppyb200_set_gemm_form) exactly,
     for the column and the four-column-quads epilogues."""
     a, b, bias = _operands(m, n, k, seed=11)
