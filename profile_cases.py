@@ -6,6 +6,8 @@ one launch of it alone.
     python profile_cases.py attention   # causal_kernel, batch 32 x 1024, 12 heads
     python profile_cases.py fc          # matmul_bf16_pair_kernel, GELU epilogue,
                                                  # GPT-2 FC (32768 x 3072 x 768)
+    python profile_cases.py proj        # matmul_bf16_pair_kernel, residual quads epilogue,
+                                         # GPT-2 proj (32768 x 768 x 3072, x += f W^T + b)
     python profile_cases.py gemm_f32    # matmul_tf32x3_pair_kernel, f32 4096^3 (after the
                                          # two split kernels of each call)
     python profile_cases.py lm_head     # matmul_bf16_pair_kernel, quads epilogue,
@@ -31,7 +33,8 @@ def main() -> None:
     from ppy_b200 import gpt2, runtime
 
     parser = argparse.ArgumentParser()
-    parser.add_argument("case", choices=["gemm", "gemm_f32", "attention", "fc", "lm_head"])
+    parser.add_argument("case", choices=["gemm", "gemm_f32", "attention", "fc", "proj",
+                                         "lm_head"])
     case = parser.parse_args().case
     runtime.init(0)
     stream = torch.cuda.Stream()
@@ -64,6 +67,14 @@ def main() -> None:
             a, b, c = main.operands
             status = lib.ppyb200_matmul_f32(a.data_ptr(), b.data_ptr(), None, c.data_ptr(),
                                             4096, 4096, 4096)
+        elif case == "proj":
+            if not hasattr(main, "operands"):
+                main.operands = (rand(32768, 3072), rand(768, 3072),
+                                 torch.zeros(768, device="cuda"),
+                                 torch.zeros(32768, 768, device="cuda"))
+            f, w, b, x = main.operands
+            status = lib.ppyb200_linear_residual(f.data_ptr(), w.data_ptr(), b.data_ptr(),
+                                                 x.data_ptr(), 32768, 768, 3072, None)
         elif case == "attention":
             if not hasattr(main, "operands"):
                 main.operands = (rand(32 * 1024, 3 * 768), rand(32 * 12 * 64, 1024),
