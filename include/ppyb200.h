@@ -109,6 +109,14 @@ int32_t ppyb200_copy_to_host(void *host_dst, const void *device_src, int64_t byt
 int32_t ppyb200_copy_rows_to_host(void *host_dst, int64_t host_pitch, const void *device_src,
                                   int64_t device_pitch, int64_t row_bytes, int64_t rows);
 
+/* A second stream of the calling thread's device for pipelining a host-memory call: fork
+ * returns it in *side after making it wait for the work already on the current stream; join
+ * makes the current stream wait for the work on it. The reference's runtime copies and
+ * launches on one synchronous path (ppy_runtime/cuda.py:194-252); built modules use these to
+ * overlap one chunk's copies with another's kernel. */
+int32_t ppyb200_fork(void **side);
+int32_t ppyb200_join(void *side);
+
 /* Translate a cudaError_t into a status, recording `what` when it is a failure. */
 int32_t ppyb200_check(int32_t cuda_error, const char *what);
 

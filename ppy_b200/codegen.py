@@ -1063,6 +1063,35 @@ def _abi_params(params: list) -> list[str]:
     return atoms
 
 
+#: Elements per slice of a pipelined host-memory call (8 MB of f32 per operand).
+PIPELINE_SLICE = 1 << 21
+
+
+def _elementwise_span(fn: P.TensorFunction, buffers: list, counts: dict) -> str | None:
+    """The element count N of a function that is elementwise over one symbolic length: one
+    binding of N from a buffer's length, no temporaries, every kernel a map over [N] of
+    contiguous (not viewed) operands, every buffer exactly N elements. Such a function gives
+    the same result run on contiguous slices of its buffers one at a time. None otherwise."""
+    if len(fn.bindings) != 1 or fn.temps or fn.dim_guards or not fn.kernels or not buffers:
+        return None
+    b = fn.bindings[0]
+    if P.numel(b.divisor) != (1, []) and P.numel(b.divisor) != (1, ()):
+        return None
+    n = f"(int64_t)1 * sym_{b.symbol}"
+    for kernel in fn.kernels:
+        if kernel.kind != "map" or P.spell_count(kernel.shape) != n or len(kernel.shape) != 1:
+            return None
+        operands = list(kernel.inputs) + [o.operand for o in kernel.outputs]
+        for o in operands:
+            if getattr(o, "view", None) is not None:
+                return None
+            if getattr(o, "source", None) == "param" and P.spell_count(o.shape) != n:
+                return None
+    if any(counts.get(p.name) != n for p in buffers):
+        return None
+    return n
+
+
 def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
     launches = []
     any_status = False
@@ -1167,6 +1196,7 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
     D.append("}")
     src.exports.append("\n".join(D))
     # host ABI
+    span = _elementwise_span(fn, buffers, counts)
     H = [f'extern "C" PPYB200_EXPORT int32_t {sym}({", ".join(_abi_params(fn.params) + ["int64_t* slot"])}) {{',
          "  ppyb200_bind_device();"]
     H += G
@@ -1181,15 +1211,53 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
     conds = [f"(n_{p.name} > 0 && d_{p.name} == nullptr)" for p in buffers if p.name in counts]
     if conds:
         H.append(f"  if ({' || '.join(conds)}) status = PPY_STATUS_RAISED;")
+    indent = "  "
+    if span is not None:
+        # Elementwise over N: contiguous slices of the buffers are independent, so large calls
+        # go in slices of PIPELINE_SLICE elements over two streams -- slice s's copies in,
+        # kernel and copies out on stream s % 2 -- and the copy in of one slice overlaps the
+        # kernel and copy out of the one before (host-to-device and device-to-host are
+        # separate PCIe directions).
+        sym_n = f"sym_{fn.bindings[0].symbol}"
+        slice_args = ([f"d_{p.name} + off" for p in buffers] + ["len"]
+                      + [f"p_{p.name}" for p in scalars])
+        H.append(f"  if (status == PPY_STATUS_OK && {sym_n} >= 2 * (int64_t){PIPELINE_SLICE}) {{")
+        H.append("    void* home = ppyb200_stream();")
+        H.append("    void* side = nullptr;")
+        H.append("    status = ppyb200_fork(&side);")
+        H.append(f"    for (int64_t off = 0, k = 0; status == PPY_STATUS_OK && off < {sym_n}; "
+                 f"off += {PIPELINE_SLICE}, ++k) {{")
+        H.append(f"      const int64_t len = {sym_n} - off < (int64_t){PIPELINE_SLICE} ? "
+                 f"{sym_n} - off : (int64_t){PIPELINE_SLICE};")
+        H.append("      ppyb200_set_stream(k % 2 ? side : home);")
+        for p in buffers:
+            if p.role in ("in", "inout"):
+                H.append(f"      if (status == PPY_STATUS_OK) status = ppyb200_copy_to_device("
+                         f"d_{p.name} + off, {p.name}_ptr + off, len * (int64_t)sizeof("
+                         f"{P.ctype(p.dtype)}));")
+        H.append(f"      if (status == PPY_STATUS_OK) status = run_{sym}({', '.join(slice_args)});")
+        for p in buffers:
+            if p.role in ("out", "inout"):
+                H.append(f"      if (status == PPY_STATUS_OK) status = ppyb200_copy_to_host("
+                         f"{p.name}_ptr + off, d_{p.name} + off, len * (int64_t)sizeof("
+                         f"{P.ctype(p.dtype)}));")
+        H.append("    }")
+        H.append("    ppyb200_set_stream(home);")
+        H.append("    if (side != nullptr) { const int32_t joined = ppyb200_join(side); "
+                 "if (status == PPY_STATUS_OK) status = joined; }")
+        H.append("  } else {")
+        indent = "    "
     for p in buffers:
         if p.name in counts and p.role in ("in", "inout"):
-            H.append(f"  if (status == PPY_STATUS_OK) status = ppyb200_copy_to_device(d_{p.name}, "
+            H.append(f"{indent}if (status == PPY_STATUS_OK) status = ppyb200_copy_to_device(d_{p.name}, "
                      f"{p.name}_ptr, n_{p.name} * (int64_t)sizeof({P.ctype(p.dtype)}));")
-    H.append(f"  if (status == PPY_STATUS_OK) status = run_{sym}({', '.join(run_args)});")
+    H.append(f"{indent}if (status == PPY_STATUS_OK) status = run_{sym}({', '.join(run_args)});")
     for p in buffers:
         if p.name in counts and p.role in ("out", "inout"):
-            H.append(f"  if (status == PPY_STATUS_OK) status = ppyb200_copy_to_host({p.name}_ptr, "
+            H.append(f"{indent}if (status == PPY_STATUS_OK) status = ppyb200_copy_to_host({p.name}_ptr, "
                      f"d_{p.name}, n_{p.name} * (int64_t)sizeof({P.ctype(p.dtype)}));")
+    if span is not None:
+        H.append("  }")
     H.append("  { const int32_t synced = ppyb200_sync(); if (status == PPY_STATUS_OK) status = synced; }")
     for p in buffers:
         if p.name in counts:
@@ -1205,6 +1273,13 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
 # -- scalar functions and parallel kernels -------------------------------------------------
 
 
+#: Consecutive indices a thread hands a parallel.for/reduce body in one call. The body loops
+#: over its own [begin, end) (lower_parallel.py:141-318 gives it that shape), so a lane runs
+#: the whole run before the warp reconverges at the call's return: one index per call made
+#: every index cost the warp its longest lane's work (Collatz: path lengths differ by 10x).
+PARALLEL_RUN = 32
+
+
 def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
     caps = [f"{t} {n}" for t, n in k.captures]
     cap_names = [n for _, n in k.captures]
@@ -1217,12 +1292,13 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
              + ", ".join(caps + ["int64_t begin", "int64_t end", f"{rt} start",
                                  f"{rt}* __restrict__ partials", "int32_t* status"]) + ") {",
              f"  {rt} acc = start;",
-             "  const int64_t count = end - begin;",
-             "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < count; "
+             f"  const int64_t runs = (end - begin + {PARALLEL_RUN} - 1) / {PARALLEL_RUN};",
+             "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < runs; "
              "t += (int64_t)gridDim.x * blockDim.x) {",
-             "    const int64_t i = begin + t;",
+             f"    const int64_t i = begin + t * {PARALLEL_RUN};",
+             f"    const int64_t stop = end - i < {PARALLEL_RUN} ? end : i + {PARALLEL_RUN};",
              f"    {rt} next;",
-             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "i + 1", "acc", "&next"]) + ");",
+             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "stop", "acc", "&next"]) + ");",
              "    if (s != PPY_STATUS_OK) {",
              "      ppyb200::raise_status(status, s);",
              "      break;",
@@ -1248,7 +1324,8 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
                                                                   f"{rt} init", f"{rt}* result"]) + ") {",
              "  cudaStream_t stream = (cudaStream_t)ppyb200_stream();",
              "  if (end <= begin) { *result = init; return PPY_STATUS_OK; }",
-             f"  const int64_t parts = ppyb200_parallel_blocks(end - begin, {T});",
+             f"  const int64_t parts = ppyb200_parallel_blocks((end - begin + {PARALLEL_RUN} - 1) / "
+             f"{PARALLEL_RUN}, {T});",
              f"  {rt}* part = ({rt}*)ppyb200_scratch((parts + 1) * (int64_t)sizeof({rt}));",
              "  if (part == nullptr) return PPY_STATUS_RAISED;",
              "  int32_t* status = ppyb200_status_word();",
@@ -1268,11 +1345,12 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
     if k.kind == "for":
         L = [f"static __global__ void __launch_bounds__({T}) {k.name}_k("
              + ", ".join(caps + ["int64_t begin", "int64_t end", "int32_t* status"]) + ") {",
-             "  const int64_t count = end - begin;",
-             "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < count; "
+             f"  const int64_t runs = (end - begin + {PARALLEL_RUN} - 1) / {PARALLEL_RUN};",
+             "  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < runs; "
              "t += (int64_t)gridDim.x * blockDim.x) {",
-             "    const int64_t i = begin + t;",
-             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "i + 1"]) + ");",
+             f"    const int64_t i = begin + t * {PARALLEL_RUN};",
+             f"    const int64_t stop = end - i < {PARALLEL_RUN} ? end : i + {PARALLEL_RUN};",
+             f"    const int32_t s = {k.body}(" + ", ".join(cap_names + ["i", "stop"]) + ");",
              "    if (s != PPY_STATUS_OK) {",
              "      ppyb200::raise_status(status, s);", "      break;", "    }", "  }", "}"]
         extra_params, extra_args = [], []
@@ -1296,7 +1374,9 @@ def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:
          "  if (end <= begin) return PPY_STATUS_OK;",
          "  int32_t* status = ppyb200_status_word();",
          "  if (status == nullptr) return PPY_STATUS_RAISED;",
-         f"  const int64_t blocks = ppyb200_parallel_blocks(end - begin, {T});",
+         ("  const int64_t blocks = ppyb200_parallel_blocks("
+          + (f"(end - begin + {PARALLEL_RUN} - 1) / {PARALLEL_RUN}" if k.kind == "for"
+             else "end - begin") + f", {T});"),
          f"  {k.name}_k<<<(unsigned)blocks, {T}, 0, stream>>>(" + ", ".join(
              cap_names + ["begin", "end"] + extra_args + ["status"]) + ");",
          "  ppyb200_count_launches(1);",

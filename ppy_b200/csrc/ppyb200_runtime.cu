@@ -37,6 +37,8 @@ struct StreamState {
 struct DeviceState {
   bool ready = false;
   cudaStream_t stream = nullptr;
+  cudaStream_t side = nullptr;         // second stream of host-memory pipelines
+  cudaEvent_t forked = nullptr, joined = nullptr;
   int sm_count = 0;
   std::map<void*, StreamState> streams;           // keyed by cudaStream_t
   std::map<int64_t, std::vector<void*>> free_buffers;  // size class -> buffers
@@ -297,6 +299,41 @@ int32_t ppyb200_copy_rows_to_host(void* host_dst, int64_t host_pitch, const void
   return check(cudaMemcpy2DAsync(host_dst, (size_t)host_pitch, device_src, (size_t)device_pitch,
                                  (size_t)row_bytes, (size_t)rows, cudaMemcpyDeviceToHost, stream),
                "device-to-host row copy");
+}
+
+int32_t ppyb200_fork(void** side) {
+  if (side == nullptr) return fail("ppyb200_fork: no result pointer");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState* state = device_state_locked();
+  if (state == nullptr) return fail("ppyb200_fork: no device");
+  if (state->side == nullptr) {
+    int32_t s = check(cudaStreamCreateWithFlags(&state->side, cudaStreamNonBlocking),
+                      "ppyb200_fork: side stream");
+    if (s == PPYB200_OK)
+      s = check(cudaEventCreateWithFlags(&state->forked, cudaEventDisableTiming), "ppyb200_fork");
+    if (s == PPYB200_OK)
+      s = check(cudaEventCreateWithFlags(&state->joined, cudaEventDisableTiming), "ppyb200_fork");
+    if (s != PPYB200_OK) return s;
+  }
+  cudaStream_t current = current_stream_locked(state);
+  int32_t s = check(cudaEventRecord(state->forked, current), "ppyb200_fork: record");
+  if (s == PPYB200_OK)
+    s = check(cudaStreamWaitEvent(state->side, state->forked, 0), "ppyb200_fork: wait");
+  *side = reinterpret_cast<void*>(state->side);
+  return s;
+}
+
+int32_t ppyb200_join(void* side) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState* state = device_state_locked();
+  if (state == nullptr) return fail("ppyb200_join: no device");
+  if (side == nullptr || side != reinterpret_cast<void*>(state->side))
+    return fail("ppyb200_join: not this device's side stream");
+  int32_t s = check(cudaEventRecord(state->joined, state->side), "ppyb200_join: record");
+  if (s == PPYB200_OK)
+    s = check(cudaStreamWaitEvent(current_stream_locked(state), state->joined, 0),
+              "ppyb200_join: wait");
+  return s;
 }
 
 int32_t ppyb200_check(int32_t cuda_error, const char* what) {

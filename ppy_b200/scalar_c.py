@@ -115,10 +115,13 @@ def _is_ptr(t) -> bool:
 class _FunctionEmitter:
     """One IR function as C++ (host or device flavour)."""
 
-    def __init__(self, owner: "ScalarEmitter", function, device: bool) -> None:
+    def __init__(self, owner: "ScalarEmitter", function, device: bool,
+                 span: tuple[int, int] | None = None) -> None:
         self.owner = owner
         self.function = function
         self.device = device
+        # for the body of a parallel.for/reduce: the positions of its (begin, end) params
+        self.span = span
         self.names: dict[int, str] = {}
         self.decls: list[str] = []
         self.lines: list[str] = []
@@ -182,7 +185,9 @@ class _FunctionEmitter:
                     self.name(argument)
         # Device code bounds every loop: a header reached more than PPYB200_LOOP_LIMIT
         # times in one call returns PPY_STATUS_RAISED instead of spinning forever (a
-        # body such as Collatz never ends for a start <= 0, on the CPU as here).
+        # body such as Collatz never ends for a start <= 0, on the CPU as here). A
+        # parallel body called on a run of indices [begin, end) gets the bound times the
+        # run's length: the same allowance per index.
         index = {id(b): i for i, b in enumerate(blocks)}
         headers = set()
         if self.device:
@@ -195,12 +200,19 @@ class _FunctionEmitter:
         for block in blocks:
             body.append(f"{self.labels[id(block)]}:;")
             if id(block) in headers:
-                body.append("  if (++loop_trips > PPYB200_LOOP_LIMIT) return PPY_STATUS_RAISED;")
+                body.append("  if (++loop_trips > trip_limit) return PPY_STATUS_RAISED;")
             for op in block.operations:
                 body.extend("  " + line for line in self.op(op))
         text = [head + " {"]
         if headers:
-            text.append("  uint32_t loop_trips = 0;")
+            text.append("  uint64_t loop_trips = 0;")
+            if self.span is not None:
+                params = [f"{self.names[id(a)]}_in" for a in fn.entry.arguments]
+                b, e = (params[i] for i in self.span)
+                text.append(f"  const uint64_t trip_limit = (uint64_t)PPYB200_LOOP_LIMIT * "
+                            f"(uint64_t)({e} > {b} ? {e} - {b} : 1);")
+            else:
+                text.append("  const uint64_t trip_limit = PPYB200_LOOP_LIMIT;")
         text += ["  " + d for d in self.decls]
         text += ["  " + c for c in entry_copies]
         text += [f"  goto {self.labels[id(blocks[0])]};"]
@@ -457,19 +469,23 @@ class ScalarEmitter:
     def host_name(function) -> str:
         return f"host_{function.name}"
 
-    def device_function(self, function) -> str:
+    def device_function(self, function, span: tuple[int, int] | None = None) -> str:
         cname = f"dev_{function.name}"
         if function.name in self.device_done:
             return cname
         self.device_done[function.name] = cname
-        text = _FunctionEmitter(self, function, device=True).emit(cname)
+        text = _FunctionEmitter(self, function, device=True, span=span).emit(cname)
         self.device_sources.append(text)
         return cname
 
     def parallel(self, emitter: _FunctionEmitter, op) -> list[str]:
         callee = self.module.functions[op.attributes["callee"].name]
-        body = self.device_function(callee)
         kind = op.local_name if hasattr(op, "local_name") else op.name.split(".", 1)[1]
+        # for and reduce bodies loop over their own [begin, end): the kernel hands them runs
+        # of indices; a map body takes one index
+        n = len(callee.params)
+        span = {"for": (n - 2, n - 1), "reduce": (n - 3, n - 2)}.get(kind)
+        body = self.device_function(callee, span)
         operands = list(op.operands)
         trailing = {"for": 2, "reduce": 3, "map": 3}[kind]
         captures = operands[: len(operands) - trailing]

@@ -340,3 +340,27 @@ def test_math_domain_guard_takes_the_fallback(rt):
     assert module.pmath_asin_table(out, 0, 8).status == int(d["asin_bad_status"]) == 1
     # the status word is per call: the next call is clean
     assert module.pmath_asin_table(out, 0, 5).status == 0
+
+
+def test_host_memory_call_in_slices_matches_the_device_call(rt):
+    """An elementwise function called with host memory runs in slices of 2^21 elements over
+    two streams (copies in, kernel, copies out per slice) once it has at least two slices:
+    the outputs equal the device entry point's bit for bit, a ragged last slice included,
+    from pinned and from pageable host memory."""
+    module = _load(rt, "gelu")
+    n = 5 * (1 << 21) + 123
+    rng = np.random.default_rng(21)
+    a, b, c = (rng.uniform(-4, 4, n).astype(np.float32) for _ in range(3))
+    ta, tb, tc = (torch.from_numpy(x).cuda() for x in (a, b, c))
+    want = torch.empty_like(ta)
+    assert module.device.gelu_chain(ta, tb, tc, want).status == 0
+    torch.cuda.synchronize()
+    want = want.cpu().numpy()
+    pageable = np.full(n, np.nan, np.float32)
+    assert module.gelu_chain(a, b, c, pageable).status == 0
+    assert np.array_equal(pageable, want)
+    pa, pb, pc = (torch.from_numpy(x).pin_memory() for x in (a, b, c))
+    pinned = torch.full((n,), float("nan")).pin_memory()
+    assert module.gelu_chain(pa, pb, pc, pinned).status == 0
+    assert np.array_equal(pinned.numpy(), want)
+    within(want[: 1 << 16], oracle.gelu_chain(a[: 1 << 16], b[: 1 << 16], c[: 1 << 16]))
