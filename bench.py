@@ -731,12 +731,15 @@ class Gpt2(Workload):
         peak = peaks["bf16_tflops_sustained"]
         forward_tflops = self.gpt2.sequence_flops(self.gpt2.GPT2_124M, self.ids.shape[0],
                                                   self.LENGTH) / (kernel_ms / 1e3) / 1e12
-        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        line = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": traffic(name),
                 "peak_source": f"{peaks['source']} cuBLAS bf16 (sustained)", "kernel": name,
                 "kernel_ms": ms / count, "forward_ms": kernel_ms,
                 "forward_tflops": forward_tflops, "forward_frac": forward_tflops / peak,
                 "breakdown_ms": {k: round(v[1], 3) for k, v in table.items()}}
+        if self.dist.world == 1:
+            line["like_for_like"] = torch_bf16_forward_ms(self.model, self.dids)
+        return line
 
     def cpu_step(self, threads: int, oracle) -> float:
         import torch
@@ -759,6 +762,68 @@ class Gpt2(Workload):
         ref = self.cpu_out[0].double()
         scale = torch_max(ref.abs(), ref.pow(2).mean().sqrt())
         return float(((got - ref).abs() / scale).max())
+
+
+def torch_bf16_forward_ms(model, ids, steps: int = 5) -> dict:
+    """The same GPT-2 forward written with torch's own bf16 operators -- cuBLAS GEMMs through
+    F.linear, F.scaled_dot_product_attention (its fused flash kernel), F.layer_norm and
+    F.gelu -- on the same weights and ids: the like-for-like comparison a torch user would
+    run. Eager, and replayed from a CUDA graph; bf16 logits (what torch gives for bf16
+    operands). A measurement beside the product path, not part of it."""
+    import torch
+    import torch.nn.functional as F
+
+    cfg = model.config
+    c, heads, hd = cfg.width, cfg.heads, cfg.head_dim
+    blocks = [{k: (v.to(torch.bfloat16) if v.dtype != torch.bfloat16 else v)
+               for k, v in blk.items()} for blk in model.blocks]
+    lnf_g, lnf_b = model.lnf_g.to(torch.bfloat16), model.lnf_b.to(torch.bfloat16)
+
+    def forward(tokens):
+        b, n = tokens.shape
+        x = model.wte[tokens] + model.wpe[:n]
+        for blk in blocks:
+            h = F.layer_norm(x, (c,), blk["ln1_g"], blk["ln1_b"], 1e-5)
+            q, k, v = F.linear(h, blk["w_qkv"], blk["b_qkv"]).split(c, dim=-1)
+            shape = lambda t: t.view(b, n, heads, hd).transpose(1, 2)  # noqa: E731
+            a = F.scaled_dot_product_attention(shape(q), shape(k), shape(v), is_causal=True)
+            x = x + F.linear(a.transpose(1, 2).reshape(b, n, c), blk["w_o"], blk["b_o"])
+            h = F.layer_norm(x, (c,), blk["ln2_g"], blk["ln2_b"], 1e-5)
+            f = F.gelu(F.linear(h, blk["w_fc"], blk["b_fc"]), approximate="tanh")
+            x = x + F.linear(f, blk["w_proj"], blk["b_proj"])
+        return F.layer_norm(x, (c,), lnf_g, lnf_b, 1e-5) @ model.wte.t()
+
+    def timed(fn) -> float:
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / steps
+
+    with torch.no_grad():
+        eager = timed(lambda: forward(ids))
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            forward(ids)
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(graph):
+            out = forward(ids)
+        replayed = timed(graph.replay)
+        del out, graph
+    torch.cuda.empty_cache()
+    tokens = ids.numel()
+    return {"torch_bf16_eager_ms": eager, "torch_bf16_graph_ms": replayed,
+            "torch_bf16_graph_tokens_per_s": tokens / (replayed / 1e3),
+            "what": "the same forward with torch's bf16 operators (cuBLAS F.linear, SDPA flash "
+                    "attention, layer_norm, gelu), bf16 logits, same weights and ids, on this "
+                    "GPU"}
 
 
 def torch_max(a, b):
