@@ -1277,7 +1277,7 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
 #: over its own [begin, end) (lower_parallel.py:141-318 gives it that shape), so a lane runs
 #: the whole run before the warp reconverges at the call's return: one index per call made
 #: every index cost the warp its longest lane's work (Collatz: path lengths differ by 10x).
-PARALLEL_RUN = 32
+PARALLEL_RUN = 1
 
 
 def _parallel_kernel(k: ParallelKernel, src: _Source) -> None:

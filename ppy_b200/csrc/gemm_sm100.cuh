@@ -37,6 +37,10 @@
 namespace ppyb200 {
 namespace gemm {
 
+using ppyb200::add2;
+using ppyb200::f2;
+using ppyb200::unf2;
+
 constexpr int BM = 128;
 constexpr int BN = 256;  // tile width; 192 where N is a multiple of 192 (pick_tile_n)
 constexpr int BK = 64;  // 64 bf16 = 128 bytes: one swizzle row
@@ -273,6 +277,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.ld without the wait: the 32 registers are not to be read before tmem_ld_wait(r),
+// which takes them as in/out operands so that every use of them is ordered after it.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]),
+                 "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]),
+                 "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -379,11 +411,16 @@ struct BiasQuads {
     if (col + 4 <= n) {
       const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col))
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      const uint64_t b01 = f2(b.x, b.y), b23 = f2(b.z, b.w);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i < count)
-          __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc),
-                 make_float4(v[i].x + b.x, v[i].y + b.y, v[i].z + b.z, v[i].w + b.w));
+      for (int i = 0; i < 8; ++i) {
+        if (i < count) {
+          float4 r;
+          unf2(add2(f2(v[i].x, v[i].y), b01), r.x, r.y);
+          unf2(add2(f2(v[i].z, v[i].w), b23), r.z, r.w);
+          __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc), r);
+        }
+      }
       return;
     }
 #pragma unroll
@@ -440,78 +477,90 @@ template <int TBN, class Epi>
 __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows)[EPI_PITCH],
                                               uint32_t acc, int half, int lane, int64_t row0,
                                               int64_t col0, int64_t rows, int64_t n) {
-  if constexpr (takes_lines<Epi>::value) {
-    static_assert(TBN % 128 == 0, "the lines form takes pairs of 32-column chunks per half");
-    uint4* line = reinterpret_cast<uint4*>(&stage_rows[0][0]);  // 32 rows x 8 slots of 16 B
-    const int slot = lane & 7;
-#pragma unroll 1
-    for (int c2 = 0; c2 < TBN / 64; c2 += 2) {
-      const int chunk = half * (TBN / 64) + c2;
-      const int64_t col = col0 + chunk * 32;  // the line's first column (N % 64 == 0: whole)
-      if constexpr (has_is_line<Epi>::value) {
-        if (!epi.is_line(col)) {  // the same for the whole warp: it depends on col alone
-#pragma unroll 1
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t r[32];
-            tmem_ld32(acc + (uint32_t)((chunk + h2) * 32), r);
-            const int64_t c = col + 32 * h2;
-            if (lane < rows && c < n) {
-              float v[32];
+  // The warp's half is NC chunks of 32 columns, taken as a stream: the TMEM load of chunk
+  // c + 1 is in flight while chunk c is turned and stored (one 32-column load ahead; the
+  // loads were one round trip each, back to back with the stores, in a warp that is one of
+  // two on its sub-partition).
+  // An epilogue that mixes line and row stores (QKV's v columns) keeps the load just before
+  // each chunk: its registers do not hold a second chunk without spilling.
+  constexpr int NC = TBN / 64;
+  constexpr bool ahead = !has_is_line<Epi>::value;
+  const int base = half * NC;
+  uint32_t r[32], next[32];
+  uint32_t pk0[16];  // the lines form: the first chunk of a pair, packed
+  if constexpr (ahead) {
+    tmem_ld32_async(acc + (uint32_t)(base * 32), r);
+    tmem_ld_wait(r);
+  }
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-              epi.store_row(v, row0 + lane, c, n - c < 32 ? n - c : 32);
-            }
+  for (int c = 0; c < NC; ++c) {
+    const int chunk = base + c;
+    if constexpr (ahead) {
+      if (c + 1 < NC) tmem_ld32_async(acc + (uint32_t)((chunk + 1) * 32), next);
+    } else {
+      tmem_ld32_async(acc + (uint32_t)(chunk * 32), r);
+      tmem_ld_wait(r);
+    }
+    if constexpr (takes_lines<Epi>::value) {
+      static_assert(NC % 2 == 0, "the lines form takes pairs of 32-column chunks per half");
+      uint4* line = reinterpret_cast<uint4*>(&stage_rows[0][0]);  // 32 rows x 8 slots of 16 B
+      const int64_t col = col0 + (chunk & ~1) * 32;  // the line's first column (N % 64 == 0)
+      bool as_line = true;
+      if constexpr (has_is_line<Epi>::value) {
+        as_line = epi.is_line(col);  // the same for the whole warp: it depends on col alone
+        if (!as_line) {
+          const int64_t cc = col0 + chunk * 32;
+          if (lane < rows && cc < n) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            epi.store_row(v, row0 + lane, cc, n - cc < 32 ? n - cc : 32);
           }
-          continue;
         }
       }
-      uint32_t pk0[16], pk1[16];
-      {
-        uint32_t r[32];
+      if (!as_line) {
+        // stored by rows above
+      } else if ((c & 1) == 0) {
         float v[32];
-        tmem_ld32(acc + (uint32_t)(chunk * 32), r);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         if (col < n) epi.pack32(v, col, pk0);
-        tmem_ld32(acc + (uint32_t)(chunk * 32 + 32), r);
+      } else {
+        uint32_t pk1[16];
+        {
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (col < n) epi.pack32(v, col + 32, pk1);
-      }
-      if (col < n) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          line[lane * 8 + (q ^ (lane & 7))] =
-              make_uint4(pk0[4 * q], pk0[4 * q + 1], pk0[4 * q + 2], pk0[4 * q + 3]);
-          line[lane * 8 + ((q + 4) ^ (lane & 7))] =
-              make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (col < n) epi.pack32(v, col + 32, pk1);
         }
-      }
-      __syncwarp();
-      if (col < n) {
-        uint4 v[8];
+        const int slot = lane & 7;
+        if (col < n) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int rr = (lane >> 3) + 4 * i;
-          v[i] = line[rr * 8 + (slot ^ (rr & 7))];
+          for (int q = 0; q < 4; ++q) {
+            line[lane * 8 + (q ^ (lane & 7))] =
+                make_uint4(pk0[4 * q], pk0[4 * q + 1], pk0[4 * q + 2], pk0[4 * q + 3]);
+            line[lane * 8 + ((q + 4) ^ (lane & 7))] =
+                make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
+          }
         }
+        __syncwarp();
+        if (col < n) {
+          uint4 v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int rr = (lane >> 3) + 4 * i;
-          if (rr < rows)
-            *reinterpret_cast<uint4*>(epi.out + (row0 + rr) * epi.ldo + col + 8 * slot) = v[i];
+          for (int i = 0; i < 8; ++i) {
+            const int rr = (lane >> 3) + 4 * i;
+            v[i] = line[rr * 8 + (slot ^ (rr & 7))];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = (lane >> 3) + 4 * i;
+            if (rr < rows)
+              *reinterpret_cast<uint4*>(epi.out + (row0 + rr) * epi.ldo + col + 8 * slot) = v[i];
+          }
         }
+        __syncwarp();
       }
-      __syncwarp();
-    }
-    return;
-  }
-#pragma unroll 1
-  for (int c4 = 0; c4 < TBN / 64; ++c4) {
-    const int chunk = half * (TBN / 64) + c4;
-    uint32_t r[32];
-    tmem_ld32(acc + (uint32_t)(chunk * 32), r);
-    if constexpr (takes_rows<Epi>::value) {
+    } else if constexpr (takes_rows<Epi>::value) {
       // lane holds row (row0 + lane), columns chunk*32 .. +31, as the epilogue takes them
       const int64_t col = col0 + chunk * 32;
       if (lane < rows && col < n) {
@@ -541,7 +590,7 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows
       // rows (lane >> 3) + 4 i inside C: i < (rows - (lane >> 3) + 3) / 4
       const int count = rows > (lane >> 3) ? (int)((rows - (lane >> 3) + 3) / 4) : 0;
       if (col < n && count > 0) epi.store_quads(v, row0 + (lane >> 3), count < 8 ? count : 8, col);
-    } else if constexpr (!takes_lines<Epi>::value) {
+    } else {
       // lane holds row (row0 + lane), columns chunk*32 .. +31: turn it through shared
       // memory so that lane j then holds column chunk*32 + j of all 32 rows
 #pragma unroll
@@ -555,6 +604,13 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, float (*stage_rows
         epi.store_column(column, row0, col, rows);
       }
       __syncwarp();
+    }
+    if constexpr (ahead) {
+      if (c + 1 < NC) {
+        tmem_ld_wait(next);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = next[j];
+      }
     }
   }
 }
