@@ -37,10 +37,6 @@
 namespace ppyb200 {
 namespace gemm {
 
-using ppyb200::add2;
-using ppyb200::f2;
-using ppyb200::unf2;
-
 constexpr int BM = 128;
 constexpr int BN = 256;  // tile width; 192 where N is a multiple of 192 (pick_tile_n)
 constexpr int BK = 64;  // 64 bf16 = 128 bytes: one swizzle row
@@ -411,16 +407,11 @@ struct BiasQuads {
     if (col + 4 <= n) {
       const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + col))
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint64_t b01 = f2(b.x, b.y), b23 = f2(b.z, b.w);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (i < count) {
-          float4 r;
-          unf2(add2(f2(v[i].x, v[i].y), b01), r.x, r.y);
-          unf2(add2(f2(v[i].z, v[i].w), b23), r.z, r.w);
-          __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc), r);
-        }
-      }
+      for (int i = 0; i < 8; ++i)
+        if (i < count)
+          __stcs(reinterpret_cast<float4*>(p + 4 * i * ldc),
+                 make_float4(v[i].x + b.x, v[i].y + b.y, v[i].z + b.z, v[i].w + b.w));
       return;
     }
 #pragma unroll

@@ -253,17 +253,12 @@ struct LinearResidualQuads {  // ld % 4 == 0, N % 4 == 0, residual and bias 16-b
     for (int i = 0; i < 8; ++i)
       old[i] = i < count ? *reinterpret_cast<const float4*>(p + 4 * i * ld)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
-    // old + (acc + bias), the pairs on the paired FP32 adds (each rounded as the scalar add)
-    const uint64_t b01 = f2(b.x, b.y), b23 = f2(b.z, b.w);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < count) {
-        float4 r;
-        unf2(add2(f2(old[i].x, old[i].y), add2(f2(v[i].x, v[i].y), b01)), r.x, r.y);
-        unf2(add2(f2(old[i].z, old[i].w), add2(f2(v[i].z, v[i].w), b23)), r.z, r.w);
-        *reinterpret_cast<float4*>(p + 4 * i * ld) = r;
-      }
-    }
+    for (int i = 0; i < 8; ++i)
+      if (i < count)
+        *reinterpret_cast<float4*>(p + 4 * i * ld) =
+            make_float4(old[i].x + (v[i].x + b.x), old[i].y + (v[i].y + b.y),
+                        old[i].z + (v[i].z + b.z), old[i].w + (v[i].w + b.w));
   }
 };
 
