@@ -6,9 +6,11 @@
 //   S_t = Q_t K^T    tcgen05.mma M=128 N=128 K=64 into TMEM (128 columns per query tile)
 //   softmax          warpgroup t (4 warps), one query row per thread: tcgen05.ld of its S row,
 //                    causal mask on the diagonal tile, P = 2^((S - m) * scale * log2 e) rounded
-//                    to bf16 into shared memory (128-byte swizzled K-major: the A operand of the
-//                    next product), running sum in f32
-//   O_t += P V       tcgen05.mma M=128 N=64 K=128 into TMEM (64 columns per query tile)
+//                    to bf16 and stored back into TMEM with tcgen05.st (64 columns of bf16
+//                    pairs per query tile: the A operand of the next product, which takes it
+//                    from TMEM -- no shared-memory round trip), running sum in f32
+//   O_t += P V       tcgen05.mma M=128 N=64 K=128, A from TMEM, into TMEM (64 columns per
+//                    query tile)
 // and at the end O_t / sum goes out as bf16 rows of the merged-heads output. The two
 // warpgroups work on their tiles at the same time (two softmax warps per SM sub-partition),
 // and the tensor core takes the products of one while the other computes.
@@ -20,10 +22,13 @@
 //
 //   warps 0-7  softmax (warpgroup t = warps 4t..4t+3; warp w reads TMEM lanes 32 (w % 4)...)
 //   warp 8     one thread: TMA loads of the Q tiles (once per item), K and V^T (3-deep ring)
-//   warp 9     one thread: the MMAs and their commits; the warp owns the TMEM allocation
-// Operands are all K-major with the 128-byte swizzle: Q and K straight from the QKV projection
-// output [tokens, 3 * width]; V from a transposed copy V^T [batch * heads * 64, length] that
-// the QKV projection's epilogue writes beside it (keys contiguous).
+//   warp 9     one thread: the MMAs of query tile 0 and their commits; the warp owns the TMEM
+//              allocation
+//   warp 10    one thread: the MMAs of query tile 1 (a single issuer serialised the two tiles'
+//              waits: 4500 cycles per key tile against about 1500 of tensor-core work)
+// Shared-memory operands are all K-major with the 128-byte swizzle: Q and K straight from the
+// QKV projection output [tokens, 3 * width]; V from a transposed copy V^T [batch * heads * 64,
+// length] that the QKV projection's epilogue writes beside it (keys contiguous).
 //
 // Every mbarrier wait is bounded as in the matmul kernel: on giving up the CTA raises the call's
 // status word, every role leaves its loops, copies and MMAs in flight are drained and the TMEM
@@ -57,13 +62,20 @@ constexpr int BM = 128;        // queries per query tile
 constexpr int BN = 128;        // keys per key tile
 constexpr int KV_STAGES = 3;
 constexpr int LOADER_WARP = 8, MMA_WARP = 9;
-constexpr int THREADS = 320;   // warps 0-7 softmax, 8 loader, 9 MMA
+constexpr int THREADS = 384;   // warps 0-7 softmax, 8 loader, 9 and 10 MMA, 11 idle
+// Registers per thread after the split (setmaxnreg): the two softmax warpgroups hold a
+// 128-score row each and take what the third (one loading thread, two issuing) gives up. The
+// launch holds LAUNCH_REGS x 384; the split must not ask for more (launch() checks the
+// compiled count before the first launch: an increase the pool cannot meet would never return).
+constexpr uint32_t LAUNCH_REGS = 168, SOFTMAX_REGS = 224, SUPPORT_REGS = 56;
+static_assert(2 * 128 * SOFTMAX_REGS + 128 * SUPPORT_REGS <= THREADS * LAUNCH_REGS,
+              "register split above the launch's registers");
 constexpr int Q_BYTES = BM * D * 2;        // [128][64] bf16, one swizzle atom wide
 constexpr int K_BYTES = BN * D * 2;        // [128 keys][64 d]
 constexpr int V_BYTES = 2 * D * 64 * 2;    // two [64 d][64 keys] halves of V^T
-constexpr int P_BYTES = 2 * BM * 64 * 2;   // two [128 q][64 keys] halves of P
-constexpr int TMEM_COLS = 512;             // S_0 [0,128), S_1 [128,256), O_0, O_1 [256,384)
-constexpr uint32_t O_COL = 256;
+constexpr int TMEM_COLS = 512;             // S_0 [0,128), S_1 [128,256), O_0, O_1 [256,384),
+constexpr uint32_t O_COL = 256;            // P_0, P_1 [384,512)
+constexpr uint32_t P_COL = 384;            // P_t: 128 bf16 keys a row, two to a column
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr float RESCALE_LOG2 = 8.f;        // the running max moves by more than this, or stays
 
@@ -77,16 +89,22 @@ struct Shared {
   alignas(1024) uint8_t q[2][Q_BYTES];
   alignas(1024) uint8_t k[KV_STAGES][K_BYTES];
   alignas(1024) uint8_t v[KV_STAGES][V_BYTES];
-  alignas(1024) uint8_t p[2][P_BYTES];
   alignas(8) uint64_t q_full, q_empty;
   alignas(8) uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
   alignas(8) uint64_t s_full[2], s_free[2];
   alignas(8) uint64_t p_full[2];
   alignas(8) uint64_t o_done[2];
-  alignas(8) uint64_t drain;
+  alignas(8) uint64_t drain[2];
   uint32_t tmem_base;
   int abort;
 };
+
+__device__ __forceinline__ void support_registers() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(SUPPORT_REGS));
+}
+__device__ __forceinline__ void softmax_registers() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(SOFTMAX_REGS));
+}
 
 __device__ __forceinline__ bool wait(Shared& s, uint64_t* bar, uint32_t parity, int32_t* status) {
   for (uint32_t tries = 0; tries < WAIT_LIMIT; ++tries) {
@@ -132,6 +150,17 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t adesc, uint64_t bd
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// The same product with A (M x 16, bf16, K-major) from tensor memory: lane m of `tmem_a` holds
+// row m, eight 32-bit columns of two bf16 each (element 2c in the low half of column c).
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void commit(uint64_t* bar) {
@@ -181,13 +210,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+// 16 columns of this thread's TMEM lane from w (tcgen05.wait::st before they are read)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* w) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]),
+      "r"(w[8]), "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]),
+      "r"(w[15])
+      : "memory");
 }
 
-// byte offset of (row, 16-byte chunk) in a 1024-byte-aligned [rows][64] bf16 tile, 128B swizzle
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t pack(float lo, float hi) {
@@ -240,10 +275,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
-    mbar_init(&s.q_empty, 1);
+    mbar_init(&s.q_empty, 2);
     for (int i = 0; i < KV_STAGES; ++i) {
       mbar_init(&s.kv_full[i], 1);
-      mbar_init(&s.kv_empty[i], 1);
+      mbar_init(&s.kv_empty[i], 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.s_full[i], 1);
@@ -251,7 +286,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s.p_full[i], 4);
       mbar_init(&s.o_done[i], 1);
     }
-    mbar_init(&s.drain, 1);
+    mbar_init(&s.drain[0], 1);
+    mbar_init(&s.drain[1], 1);
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -268,8 +304,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   // the set-up above overlaps the previous kernel; its results are needed from here on
   pdl_wait();
   pdl_trigger();
-
+  // Each role takes its share of the register split first, with the whole warp (the four
+  // warps of a warpgroup ask for the same count).
   if (warp == LOADER_WARP) {
+    support_registers();
     if (lane == 0) {
       // ---- loader
       uint64_t kv = 0, qi = 0;
@@ -306,81 +344,85 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_drain_wait(&s.kv_full[j % KV_STAGES], (uint32_t)((j / KV_STAGES) & 1));
       if (qi > 0) mbar_drain_wait(&s.q_full, (uint32_t)((qi - 1) & 1));
     }
-  } else if (warp == MMA_WARP) {
+  } else if (warp == MMA_WARP || warp == MMA_WARP + 1) {
+    support_registers();
     if (lane == 0) {
-      // ---- MMA issuer. Step j: S_0(j), S_1(j), then O_0 += P_0(j-1) V, O_1 += P_1(j-1) V.
-      uint64_t kv = 0, qi = 0;
-      uint64_t sc[2] = {0, 0}, pc[2] = {0, 0};  // S and PV products issued per query tile
+      // ---- MMA issuers: warp MMA_WARP + t issues the products of query tile t, so that one
+      // tile's waits never hold up the other's products. Step j: S_t(j), then
+      // O_t += P_t(j-1) V(j-1). tcgen05.commit tracks the products of the committing thread,
+      // so the stage and Q barriers take one arrival from each issuer: a commit after its
+      // products, or a plain arrival for a key tile (or a Q tile) it has no product of --
+      // given only after waiting for that stage's (that Q's) load, so that the arrival falls
+      // in the phase it belongs to.
+      const int t = warp - MMA_WARP;
+      uint64_t kv = 0, qi = 0, sc = 0, pc = 0;  // S and PV products issued for this tile
       bool ok = true;
       int64_t round = 0;
       for (int64_t i = snake_item(0); i < items && ok; i = snake_item(++round), ++qi) {
         const Item it = item_of(i, bh, heads, q_tiles);
-        const int64_t n_t[2] = {2 * it.p + 1, it.has1 ? 2 * it.p + 2 : 0};
-        const int64_t tiles = it.has1 ? n_t[1] : n_t[0];
+        const int64_t tiles = it.has1 ? 2 * it.p + 2 : 2 * it.p + 1;  // key tiles loaded
+        const int64_t mine = t == 0 ? 2 * it.p + 1 : (it.has1 ? 2 * it.p + 2 : 0);
         if (!wait(s, &s.q_full, (uint32_t)(qi & 1), status)) break;
         tc_fence_after();
+        if (mine == 0) mbar_arrive(&s.q_empty);
         for (int64_t j = 0; j <= tiles && ok; ++j) {
-          if (j < tiles) {
+          if (j < mine) {
             const uint64_t kj = kv + (uint64_t)j;
             const int st = (int)(kj % KV_STAGES);
-            if (!wait(s, &s.kv_full[st], (uint32_t)((kj / KV_STAGES) & 1), status)) {
+            if (!wait(s, &s.kv_full[st], (uint32_t)((kj / KV_STAGES) & 1), status) ||
+                !wait(s, &s.s_free[t], (uint32_t)((sc & 1) ^ 1), status)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint64_t kdesc = smem_desc(s.k[st]);
+            const uint64_t qdesc = smem_desc(s.q[t]);
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              if (!ok || j >= n_t[t]) continue;
-              if (!wait(s, &s.s_free[t], (uint32_t)((sc[t] & 1) ^ 1), status)) {
-                ok = false;
-                continue;
-              }
-              tc_fence_after();
-              const uint64_t qdesc = smem_desc(s.q[t]);
-#pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk)
-                mma(tmem + (uint32_t)(t * BN), qdesc + (uint64_t)(kk * 2),
-                    kdesc + (uint64_t)(kk * 2), IDESC_S, kk > 0 ? 1u : 0u);
-              commit(&s.s_full[t]);
-              ++sc[t];
-            }
-            if (!ok) break;
-            if (j == tiles - 1) commit(&s.q_empty);
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma(tmem + (uint32_t)(t * BN), qdesc + (uint64_t)(kk * 2),
+                  kdesc + (uint64_t)(kk * 2), IDESC_S, kk > 0 ? 1u : 0u);
+            commit(&s.s_full[t]);
+            ++sc;
+            if (j == mine - 1) commit(&s.q_empty);
           }
           if (j >= 1) {
             const int64_t jp = j - 1;
             const uint64_t kj = kv + (uint64_t)jp;
             const int st = (int)(kj % KV_STAGES);
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              if (!ok || jp >= n_t[t]) continue;
-              if (!wait(s, &s.p_full[t], (uint32_t)(pc[t] & 1), status)) {
+            if (jp < mine) {
+              if (!wait(s, &s.p_full[t], (uint32_t)(pc & 1), status)) {
                 ok = false;
-                continue;
+                break;
               }
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < BN / 16; ++kk) {
                 const int half = kk >> 2, off = (kk & 3) * 2;
-                const uint64_t pdesc = smem_desc(s.p[t] + half * (P_BYTES / 2)) + (uint64_t)off;
                 const uint64_t vdesc = smem_desc(s.v[st] + half * (V_BYTES / 2)) + (uint64_t)off;
-                mma(tmem + O_COL + (uint32_t)(t * D), pdesc, vdesc, IDESC_O,
-                    (jp > 0 || kk > 0) ? 1u : 0u);
+                mma_ts(tmem + O_COL + (uint32_t)(t * D), tmem + P_COL + (uint32_t)(t * 64 + kk * 8),
+                       vdesc, IDESC_O, (jp > 0 || kk > 0) ? 1u : 0u);
               }
               commit(&s.o_done[t]);
-              ++pc[t];
+              ++pc;
+              commit(&s.kv_empty[st]);
+            } else if (jp < tiles) {
+              if (!wait(s, &s.kv_full[st], (uint32_t)((kj / KV_STAGES) & 1), status)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive(&s.kv_empty[st]);
             }
-            if (!ok) break;
-            commit(&s.kv_empty[st]);
           }
         }
         kv += (uint64_t)tiles;
       }
-      commit(&s.drain);
-      mbar_drain_wait(&s.drain, 0);
+      commit(&s.drain[t]);
+      mbar_drain_wait(&s.drain[t], 0);
     }
+  } else if (warp > MMA_WARP + 1) {
+    support_registers();  // the idle warp of the third warpgroup
   } else {
+    softmax_registers();
     // ---- softmax: warpgroup t = warp / 4 takes query tile 2p + t; thread = query row. The
     // running max m is kept in raw score units.
     const int t = warp >> 2;
@@ -388,6 +430,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_addr + (uint32_t)(t * BN);
     const uint32_t o_addr = tmem + lane_addr + O_COL + (uint32_t)(t * D);
+    const uint32_t p_addr = tmem + lane_addr + P_COL + (uint32_t)(t * 64);
     const uint64_t scale2 = f2(scale_log2, scale_log2);
     uint64_t sc = 0, pc = 0;
     bool ok = true;
@@ -438,21 +481,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         const float shift = -m * scale_log2;
         const uint64_t shift2 = f2(shift, shift);
-        uint64_t sum2[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int c = 0; c < BN; c += 2) {
-          float lo, hi;
-          unf2(fma2(f2(sv[c], sv[c + 1]), scale2, shift2), lo, hi);
-          sv[c] = ex2(lo);
-          sv[c + 1] = ex2(hi);
-          sum2[(c >> 1) & 3] = add2(sum2[(c >> 1) & 3], f2(sv[c], sv[c + 1]));
-        }
-        float s0, s1, s2, s3;
-        unf2(add2(sum2[0], sum2[1]), s0, s1);
-        unf2(add2(sum2[2], sum2[3]), s2, s3);
-        l += (s0 + s1) + (s2 + s3);
-        // P_t was read by the previous product into O_t, which the rescale below rewrites:
-        // both wait for that product
+        // P_t(j-1) was read by the previous product into O_t, which the rescale below
+        // rewrites: P_t(j) and the rescale wait for that product
         if (pc > 0) {
           if (!warp_wait(s, &s.o_done[t], (uint32_t)((pc - 1) & 1), status)) {
             ok = false;
@@ -460,20 +490,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
         }
+        uint64_t sum2[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint8_t* tile = s.p[t] + half * (P_BYTES / 2);
+        for (int quarter = 0; quarter < 4; ++quarter) {
+          // 32 probabilities, packed to bf16 pairs and stored as they are made (the scores
+          // they replace free their registers)
+          uint32_t pk[16];
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const int c = half * 64 + ch * 8;
-            uint4 packed;
-            packed.x = pack(sv[c + 0], sv[c + 1]);
-            packed.y = pack(sv[c + 2], sv[c + 3]);
-            packed.z = pack(sv[c + 4], sv[c + 5]);
-            packed.w = pack(sv[c + 6], sv[c + 7]);
-            *reinterpret_cast<uint4*>(tile + swz(row, ch)) = packed;
+          for (int c = quarter * 32; c < quarter * 32 + 32; c += 2) {
+            float lo, hi;
+            unf2(fma2(f2(sv[c], sv[c + 1]), scale2, shift2), lo, hi);
+            const float e0 = ex2(lo), e1 = ex2(hi);
+            sum2[(c >> 1) & 3] = add2(sum2[(c >> 1) & 3], f2(e0, e1));
+            pk[(c >> 1) & 15] = pack(e0, e1);
           }
+          tmem_st16(p_addr + (uint32_t)(quarter * 16), pk);
         }
+        float s0, s1, s2, s3;
+        unf2(add2(sum2[0], sum2[1]), s0, s1);
+        unf2(add2(sum2[2], sum2[3]), s2, s3);
+        l += (s0 + s1) + (s2 + s3);
         if (j > 0 && __any_sync(0xffffffffu, move)) {
           // some rows' max moved: scale those rows of O_t (the previous products' sum)
           float o[D];
@@ -487,8 +523,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c = 0; c < D / 32; ++c) tmem_st32(o_addr + (uint32_t)(c * 32), o + c * 32);
           tmem_wait_st();
         }
-        // P in shared memory (generic-proxy writes) becomes an MMA operand (async proxy)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        // P in tensor memory becomes the A operand of O_t += P V once its stores completed
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.p_full[t]);
@@ -565,12 +601,17 @@ inline cudaError_t launch(const __nv_bfloat16* qkv, const __nv_bfloat16* vt, __n
   int ready = 0;
   cudaError_t e = configured.get(
       [](int* v) {
-        *v = 1;
+        cudaFuncAttributes attributes;
+        cudaError_t r = cudaFuncGetAttributes(&attributes, causal_kernel);
+        if (r != cudaSuccess) return r;
+        // the register split needs the launch's full LAUNCH_REGS a thread
+        *v = attributes.numRegs == (int)LAUNCH_REGS ? 1 : 0;
         return cudaFuncSetAttribute(causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)shared_bytes());
       },
       &ready);
   if (e != cudaSuccess) return e;
+  if (ready != 1) return cudaErrorInvalidKernelImage;
   const int64_t items = batch * heads * ((length / BM + 1) / 2);
   const int grid = (int)(items < sm_count ? items : sm_count);
   const float scale_log2 = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
