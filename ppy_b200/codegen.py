@@ -595,9 +595,11 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
     warps = block // 32
     masked = chunks % tpr != 0
     elem_inputs = [i for i, c in enumerate(in_class) if c == "elem"]
-    # Pipelined form: persistent warps, each prefetching its next row group into shared
-    # memory (cp.async, double-buffered) while it computes the current one. It needs
-    # 16-byte chunks and a row group per warp (rows of at most 32 lanes).
+    # Pipelined form: persistent warps, each prefetching its next row groups into a ring in
+    # shared memory (bulk copies completing on an mbarrier per stage) while it computes the
+    # current one. It needs 16-byte chunks and a row group per warp (rows of at most 32
+    # lanes). A stage whose copy never completes (bounded wait) raises the status word when
+    # the call has one.
     pipelined = tpr <= 32 and elem_inputs and all(
         vec * P.size_of(kernel.inputs[i].dtype) == 16 for i in elem_inputs)
     rpw = 32 // tpr if tpr <= 32 else 1
@@ -798,41 +800,41 @@ def _row_kernel(kernel: P.RowKernel, fn: P.TensorFunction, src: _Source) -> dict
         L.append("  const int64_t stride = (int64_t)gridDim.x * WPB;")
         L.append(f"  constexpr int STAGES = {stages};")
         L.append("  unsigned char* wbuf = smem + warp * STAGES * BUF;")
-        # prefetch of one row group into buffer b: every lane copies the chunks it reads
+        # the warp's ring: a row group (RPW consecutive rows, contiguous in every input) per
+        # stage, one bulk copy per input, one mbarrier per stage
+        L.append("  __shared__ uint64_t ring[WPB][STAGES];")
+        L.append("  if ((threadIdx.x & 31) == 0) ppyb200::ring_init(ring[warp], STAGES);")
+        L.append("  __syncwarp();")
+        L.append("  uint32_t phases = 0;  // bit k: the parity stage k completes next")
+        row_bytes = sum(P.size_of(kernel.inputs[i].dtype) for i in elem_inputs)
         P_ = ["  auto prefetch = [&](int64_t g, int b) {",
-              "    const int64_t prow = g * RPW + slot;",
-              "    if (prow >= R) return;",
-              "    unsigned char* pb = wbuf + b * BUF;"]
+              "    const int64_t prow = g * RPW;",
+              "    if (prow >= R || (threadIdx.x & 31) != 0) return;",
+              "    const int64_t rows = R - prow < RPW ? R - prow : RPW;",
+              "    unsigned char* pb = wbuf + b * BUF;",
+              f"    ppyb200::ring_expect(&ring[warp][b], (uint32_t)(rows * COLS * {row_bytes}));"]
         for i in elem_inputs:
             size = P.size_of(kernel.inputs[i].dtype)
-            P_.append("    #pragma unroll")
-            P_.append("    for (int j = 0; j < NCH; ++j) {")
-            if masked:
-                P_.append("      if (j * TPR + lane >= CHUNKS) continue;")
-            P_.append(f"      ppyb200::cp_async16(pb + {seg[i]} + (slot * COLS + (int64_t)(j * TPR + lane) * VEC) * {size}, "
-                      f"in{i} + prow * COLS + (int64_t)(j * TPR + lane) * VEC);")
-            P_.append("    }")
+            P_.append(f"    ppyb200::ring_load(pb + {seg[i]}, in{i} + prow * COLS, "
+                      f"(uint32_t)(rows * COLS * {size}), &ring[warp][b]);")
         P_.append("  };")
         L.extend(P_)
-        # STAGES - 1 row groups in flight ahead of the one computed; one commit group per
-        # prefetch (empty past the end), so that wait<STAGES - 1> always means "this one"
+        # STAGES - 1 row groups in flight ahead of the one computed
         L.append("  #pragma unroll")
-        L.append("  for (int k = 0; k < STAGES - 1; ++k) {")
+        L.append("  for (int k = 0; k < STAGES - 1; ++k)")
         L.append("    if (first + k * stride < groups) prefetch(first + k * stride, k);")
-        L.append("    ppyb200::cp_async_commit();")
-        L.append("  }")
         L.append("  int b = 0;")
         L.append("  for (int64_t g = first; g < groups; g += stride, b = (b + 1) % STAGES) {")
         L.append("    const int64_t ahead = g + (STAGES - 1) * stride;")
+        L.append("    __syncwarp();  // every lane has read the stage that is refilled next")
         L.append("    if (ahead < groups) prefetch(ahead, (b + STAGES - 1) % STAGES);")
-        L.append("    ppyb200::cp_async_commit();")
-        L.append("    ppyb200::cp_async_wait<STAGES - 1>();")
+        L.append("    ppyb200::ring_wait(&ring[warp][b], (phases >> b) & 1u, status);")
+        L.append("    phases ^= 1u << b;")
         L.append("    const unsigned char* buf = wbuf + b * BUF;")
         L.append("    const int64_t row = g * RPW + slot;")
         L.append("    const bool active = row < R;")
         L.extend("    " + line for line in B)
         L.append("  }")
-        L.append("  ppyb200::cp_async_wait<0>();")
         L.append("}")
     else:
         L.append("  {")

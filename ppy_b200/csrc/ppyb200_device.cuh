@@ -279,19 +279,57 @@ namespace ppyb200 {
 
 // ---------------------------------------------------------------- async copies to shared
 
-// One 16-byte global->shared copy that completes asynchronously (cp.async, L2 only), and
-// the group fences around it: a row kernel prefetches its next row with these while it
-// computes the current one.
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+// ---- a warp's ring of row groups in shared memory, filled by bulk copies (the TMA engine:
+// one instruction per row group instead of a 16-byte copy per lane and chunk), one mbarrier a
+// stage. Measured on the [65536, 1024] f32 row group: 5.58 -> 5.75 TB/s against per-lane
+// cp.async copies.
+constexpr uint32_t RING_WAIT_LIMIT = 1u << 24;
+
+// lane 0 of the warp: `stages` barriers of one arrival each (the copies add their bytes)
+__device__ __forceinline__ void ring_init(uint64_t* bars, int stages) {
+  for (int k = 0; k < stages; ++k)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(
+        static_cast<unsigned>(__cvta_generic_to_shared(bars + k))));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
+
+// one thread: the stage's barrier expects `bytes` (the sum of the copies that follow)
+__device__ __forceinline__ void ring_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(bar))),
+               "r"(bytes)
+               : "memory");
 }
-template <int PENDING>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(PENDING) : "memory");
+
+// one thread: `bytes` (a multiple of 16) from global `src` to shared `dst`, both 16-byte
+// aligned, completing on `bar`. The proxy fence orders the warp's earlier reads of the buffer
+// (generic proxy) before the copy's writes (async proxy).
+__device__ __forceinline__ void ring_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+      "l"(src), "r"(bytes), "r"(static_cast<unsigned>(__cvta_generic_to_shared(bar)))
+      : "memory");
+}
+
+// every lane: wait (bounded) for the stage's phase of `parity`; on giving up the call's status
+// word is raised and the stage is read as it is (in bounds, not the row group)
+__device__ __forceinline__ void ring_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+  const unsigned b = static_cast<unsigned>(__cvta_generic_to_shared(bar));
+  for (uint32_t tries = 0; tries < RING_WAIT_LIMIT; ++tries) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(b), "r"(parity)
+        : "memory");
+    if (done) return;
+  }
+  if (status != nullptr) atomicMax(status, PPYB200_DEVICE_RAISED);
 }
 
 // ---- two f32 lanes in one 64-bit register, for the paired FP32 instructions of sm_100
