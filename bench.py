@@ -858,9 +858,11 @@ class Gpt2TP(Gpt2):
         cfg = super().config()
         tokens = self.ids.numel()
         if self.exchange == "nvlink":
-            exchange = (f"fused: each row-parallel GEMM's epilogue stores its f32 [{tokens}, "
-                        f"768] partial into every rank of its group of {self.tp} over NVLink, "
-                        "then a flag per rank and an in-order sum; 2 per block")
+            exchange = (f"fused reduce-scatter + all-gather over NVLink in each group of "
+                        f"{self.tp}: each row-parallel GEMM's epilogue stores the rows of the "
+                        f"f32 [{tokens}, 768] partial owned by rank s into rank s's buffer, a "
+                        "flag per rank, the owner's in-order sum of its block sent to every "
+                        "rank, a second flag round; 2 per block")
         else:
             exchange = (f"2 NCCL all-reduces (sum, f32 [{tokens}, 768]) per block inside "
                         f"each group of {self.tp}")

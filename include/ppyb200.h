@@ -278,6 +278,36 @@ int32_t ppyb200_tp_accumulate(float *x, const float *bias, const float *exchange
                               const int32_t *flags, int32_t ranks, int64_t m, int64_t n,
                               int32_t epoch, int32_t *status);
 
+/* The reduce-scatter form of the same exchange, (R - 1) / R of the partial sent twice instead
+ * of all of it R - 1 times (R = ranks). Rows split into blocks of ceil(M / R); block s belongs to
+ * rank s.
+ *
+ * ppyb200_tp_partial_reduce_scatter: as ppyb200_tp_partial_scatter, but the epilogue stores
+ * the rows of block s only, into slots[s] -- this rank's slot in rank s's exchange buffer,
+ * [ceil(M / R), N] f32.
+ * Then ppyb200_tp_signal on the first flag set.
+ *
+ * ppyb200_tp_reduce_block: waits (bounded) until flags[0..ranks) reach `epoch`, then for the
+ * rows of block `rank`: x += bias + exchange[0] + exchange[1] + ... (slot s at
+ * s * ceil(M / R) * N floats, rank order: the sum ppyb200_tp_accumulate makes), and the result
+ * into gather[s] for every s != rank (this rank's slot in rank s's gather buffer, same shape).
+ * Then ppyb200_tp_signal on the second flag set.
+ *
+ * ppyb200_tp_gather_blocks: waits (bounded) until flags[0..ranks) reach `epoch`, then copies
+ * slot s of `gathered` (this rank's gather buffer, written by rank s) into block s of x for
+ * every s != rank. `gather`/`slots` are host arrays; a wait given up raises `*status` (may be
+ * NULL) to 2 and leaves x alone. N % 4 == 0, pointers 16-byte aligned. */
+int32_t ppyb200_tp_partial_reduce_scatter(const uint16_t *a, const uint16_t *w,
+                                          float *const *slots, int32_t ranks, int64_t m,
+                                          int64_t n, int64_t k, int32_t *status);
+int32_t ppyb200_tp_reduce_block(float *x, const float *bias, const float *exchange,
+                                float *const *gather, const int32_t *flags, int32_t ranks,
+                                int32_t rank, int64_t m, int64_t n, int32_t epoch,
+                                int32_t *status);
+int32_t ppyb200_tp_gather_blocks(float *x, const float *gathered, const int32_t *flags,
+                                 int32_t ranks, int32_t rank, int64_t m, int64_t n,
+                                 int32_t epoch, int32_t *status);
+
 /* ---------------------------------------------------------------- measurement */
 
 /* The issue ceiling of the Collatz step body of the parallel.range reduction (the reference's

@@ -17,6 +17,22 @@
 // epoch E only after its own wait for E - 1, which needs every peer's flag for E - 1, which a
 // peer raises after its accumulate of E - 2 -- the last read of parity p. No load anywhere is
 // a TMA multicast: the peer traffic is plain stores from the epilogue and the flag stores.
+//
+// The reduce-scatter form sends each rank (R - 1) / R of the partial twice instead of all of
+// it R - 1 times: rows split into R blocks, block s owned by rank s.
+//
+//   ppyb200_tp_partial_reduce_scatter   the GEMM's epilogue stores the tile rows of block s
+//                                       into slot r of rank s's exchange buffer only
+//   ppyb200_tp_signal                   flags of the first round
+//   ppyb200_tp_reduce_block             waits for them; x[own block] += bias + slot 0 + slot 1
+//                                       + ... in rank order, and the summed block goes into
+//                                       slot r of every rank's gather buffer
+//   ppyb200_tp_signal                   flags of the second round
+//   ppyb200_tp_gather_blocks            waits for them; the other ranks' blocks into x
+// Each block is summed once, by its owner, in the same order as the all-slot form: the
+// residual stream stays bit-identical across the group and equal to that form's. Both buffers
+// are double-buffered by epoch parity as above: a rank writes parity p of epoch E after its
+// gather wait of E - 1, which follows every peer's reduce of E - 1 and so its reads of E - 2.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -58,6 +74,30 @@ struct PeerScatterQuads {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         if (i < count) *reinterpret_cast<float4*>(p + 4 * i * ld) = v[i];
+    }
+  }
+};
+
+// The partial product's quads, each row to the rank that owns its block (rows
+// [s * block_rows, (s + 1) * block_rows) to rank s): dst[s] is this rank's slot in rank s's
+// exchange buffer, [block_rows, ld] f32.
+struct PeerScatterBlocks {
+  static constexpr bool kQuads = true;
+  float* dst[MAX_RANKS];
+  int64_t block_rows;
+  int64_t ld;
+  __device__ __forceinline__ void store_quads(const float4 (&v)[8], int64_t row, int count,
+                                              int64_t col) const {
+    int64_t s = row / block_rows, start = s * block_rows;  // one division for the 8 rows
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i >= count) break;
+      const int64_t r = row + 4 * i;
+      while (r >= start + block_rows) {  // at most ranks - 1 steps over the 29 rows
+        ++s;
+        start += block_rows;
+      }
+      *reinterpret_cast<float4*>(dst[s] + (r - start) * ld + col) = v[i];
     }
   }
 };
@@ -146,6 +186,87 @@ __global__ void __launch_bounds__(256) tp_accumulate_kernel(
     acc.z += sum.z;
     acc.w += sum.w;
     *reinterpret_cast<float4*>(x + 4 * i) = acc;
+  }
+}
+
+// Bounded wait of one thread for flags[0..ranks) to reach `epoch`; the block follows it.
+__device__ __forceinline__ bool block_wait_flags(const int32_t* flags, int32_t ranks,
+                                                 int32_t epoch, int32_t* status) {
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    const uint64_t start = global_ns();
+    int ok = 1;
+    for (int s = 0; s < ranks && ok; ++s) {
+      while (load_acquire_sys(flags + s) < epoch) {
+        if (global_ns() - start > WAIT_NS) {
+          ok = 0;
+          break;
+        }
+        __nanosleep(200);
+      }
+    }
+    if (!ok && status != nullptr) atomicMax(status, PPYB200_DEVICE_RAISED);
+    ready = ok;
+  }
+  __syncthreads();
+  return ready != 0;
+}
+
+struct PeerBlocks {
+  float* dst[MAX_RANKS];
+};
+
+// x[rows of block `rank`] += bias + sum_s exchange[s] (rank order), after every flag reaches
+// `epoch`; the result also into gather[s] (this rank's slot in rank s's gather buffer) for
+// every s != rank. exchange: this rank's [ranks][block_rows, n] slots (peers store into it).
+__global__ void __launch_bounds__(256) tp_reduce_block_kernel(
+    float* __restrict__ x, const float* __restrict__ bias, const float* exchange, PeerBlocks gather,
+    const int32_t* flags, int32_t ranks, int32_t rank, int64_t m, int64_t n, int64_t block_rows,
+    int32_t epoch, int32_t* status) {
+  if (!block_wait_flags(flags, ranks, epoch, status)) return;
+  const int64_t first = rank * block_rows;
+  const int64_t rows = (m - first < block_rows ? m - first : block_rows);
+  if (rows <= 0) return;
+  const int64_t quads = rows * n / 4, per = n / 4, slot = block_rows * n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = *reinterpret_cast<const float4*>(x + first * n + 4 * i);
+    const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias) + i % per)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 sum = b;
+    for (int s = 0; s < ranks; ++s) {
+      const float4 p = load_peer4(exchange + s * slot + 4 * i);
+      sum.x += p.x;
+      sum.y += p.y;
+      sum.z += p.z;
+      sum.w += p.w;
+    }
+    acc.x += sum.x;
+    acc.y += sum.y;
+    acc.z += sum.z;
+    acc.w += sum.w;
+    *reinterpret_cast<float4*>(x + first * n + 4 * i) = acc;
+    for (int s = 0; s < ranks; ++s)
+      if (s != rank) *reinterpret_cast<float4*>(gather.dst[s] + 4 * i) = acc;
+  }
+}
+
+// After every flag reaches `epoch`: the blocks of the other ranks from this rank's gather
+// buffer ([ranks][block_rows, n], slot s written by rank s) into x.
+__global__ void __launch_bounds__(256) tp_gather_blocks_kernel(
+    float* __restrict__ x, const float* gathered, const int32_t* flags, int32_t ranks,
+    int32_t rank, int64_t m, int64_t n, int64_t block_rows, int32_t epoch, int32_t* status) {
+  if (!block_wait_flags(flags, ranks, epoch, status)) return;
+  const int64_t per_block = block_rows * n / 4;
+  const int64_t quads = (int64_t)ranks * per_block;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = i / per_block, q = i - s * per_block;
+    if (s == rank) continue;
+    const int64_t row = s * block_rows + (4 * q) / n;
+    if (row >= m) continue;
+    *reinterpret_cast<float4*>(x + s * block_rows * n + 4 * q) =
+        load_peer4(gathered + s * block_rows * n + 4 * q);
   }
 }
 
@@ -251,6 +372,86 @@ int32_t ppyb200_tp_accumulate(float* x, const float* bias, const float* exchange
   tp_accumulate_kernel<<<(unsigned)blocks, 256, 0, stream_now()>>>(x, bias, exchange, flags,
                                                                    ranks, m, n, epoch, status);
   return finish(cudaGetLastError(), "ppyb200_tp_accumulate", 1);
+}
+
+int32_t ppyb200_tp_partial_reduce_scatter(const uint16_t* a, const uint16_t* w,
+                                          float* const* slots, int32_t ranks, int64_t m,
+                                          int64_t n, int64_t k, int32_t* status) {
+  if (m < 0 || n < 0 || k < 0 || ranks < 1 || ranks > MAX_RANKS || slots == nullptr) {
+    ppyb200_set_error("ppyb200_tp_partial_reduce_scatter: extents >= 0 and 1 to 8 ranks");
+    return PPYB200_RAISED;
+  }
+  if (m == 0 || n == 0) return PPYB200_OK;
+  if (!ppyb200::gemm::tileable(m, n, k) || n % 4 != 0 || !aligned16(a) || !aligned16(w)) {
+    ppyb200_set_error(
+        "ppyb200_tp_partial_reduce_scatter: K % 64, N % 4 and 16-byte aligned operands");
+    return PPYB200_RAISED;
+  }
+  PeerScatterBlocks epi{};
+  for (int s = 0; s < ranks; ++s) {
+    if (slots[s] == nullptr || !aligned16(slots[s])) {
+      ppyb200_set_error("ppyb200_tp_partial_reduce_scatter: 16-byte aligned slots");
+      return PPYB200_RAISED;
+    }
+    epi.dst[s] = slots[s];
+  }
+  epi.block_rows = (m + ranks - 1) / ranks;
+  epi.ld = n;
+  cudaError_t e = ppyb200::gemm::launch(reinterpret_cast<const __nv_bfloat16*>(a),
+                                        reinterpret_cast<const __nv_bfloat16*>(w), m, n, k, epi,
+                                        status, ppyb200_sm_count(), stream_now());
+  return finish(e, "ppyb200_tp_partial_reduce_scatter", 1);
+}
+
+int32_t ppyb200_tp_reduce_block(float* x, const float* bias, const float* exchange,
+                                float* const* gather, const int32_t* flags, int32_t ranks,
+                                int32_t rank, int64_t m, int64_t n, int32_t epoch,
+                                int32_t* status) {
+  if (ranks < 1 || ranks > MAX_RANKS || rank < 0 || rank >= ranks || m < 0 || n <= 0 ||
+      n % 4 != 0 || !aligned16(x) || !aligned16(exchange) ||
+      (bias != nullptr && !aligned16(bias)) || flags == nullptr || gather == nullptr) {
+    ppyb200_set_error("ppyb200_tp_reduce_block: 1 to 8 ranks, N % 4 == 0, 16-byte aligned x, "
+                      "bias, exchange");
+    return PPYB200_RAISED;
+  }
+  if (m == 0) return PPYB200_OK;
+  PeerBlocks peers{};
+  for (int s = 0; s < ranks; ++s) {
+    if (s != rank && (gather[s] == nullptr || !aligned16(gather[s]))) {
+      ppyb200_set_error("ppyb200_tp_reduce_block: 16-byte aligned gather slots");
+      return PPYB200_RAISED;
+    }
+    peers.dst[s] = gather[s];
+  }
+  const int64_t block_rows = (m + ranks - 1) / ranks;
+  const int64_t quads = block_rows * n / 4;
+  int64_t blocks = (quads + 255) / 256;
+  const int64_t cap = (int64_t)ppyb200_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  tp_reduce_block_kernel<<<(unsigned)blocks, 256, 0, stream_now()>>>(
+      x, bias, exchange, peers, flags, ranks, rank, m, n, block_rows, epoch, status);
+  return finish(cudaGetLastError(), "ppyb200_tp_reduce_block", 1);
+}
+
+int32_t ppyb200_tp_gather_blocks(float* x, const float* gathered, const int32_t* flags,
+                                 int32_t ranks, int32_t rank, int64_t m, int64_t n,
+                                 int32_t epoch, int32_t* status) {
+  if (ranks < 1 || ranks > MAX_RANKS || rank < 0 || rank >= ranks || m < 0 || n <= 0 ||
+      n % 4 != 0 || !aligned16(x) || !aligned16(gathered) || flags == nullptr) {
+    ppyb200_set_error("ppyb200_tp_gather_blocks: 1 to 8 ranks, N % 4 == 0, 16-byte aligned "
+                      "x and gather buffer");
+    return PPYB200_RAISED;
+  }
+  if (m == 0) return PPYB200_OK;
+  const int64_t block_rows = (m + ranks - 1) / ranks;
+  const int64_t quads = (int64_t)ranks * block_rows * n / 4;
+  int64_t blocks = (quads + 255) / 256;
+  const int64_t cap = (int64_t)ppyb200_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  tp_gather_blocks_kernel<<<(unsigned)blocks, 256, 0, stream_now()>>>(
+      x, gathered, flags, ranks, rank, m, n, block_rows, epoch, status);
+  return finish(cudaGetLastError(), "ppyb200_tp_gather_blocks", 1);
 }
 
 }  // extern "C"

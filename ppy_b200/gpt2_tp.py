@@ -16,11 +16,14 @@ LM head:
     LM head          vocab-parallel: this rank's slice of the logits
 
 Two all-reduces of the f32 residual stream [tokens, 768] per block: NCCL's after each
-row-parallel GEMM (`exchange="nccl"`), or, with `exchange="nvlink"`, none at all -- the GEMM's
-epilogue stores its partial tiles straight into a slot of every rank's exchange buffer over
-NVLink (csrc/tp_exchange.cu), a flag per rank marks them complete, and each rank adds the bias
-and the slots to its residual stream in rank order (the same sum, bit for bit, on every rank). g divides 12 and the local
-widths (768/g and 3072/g) stay multiples of 64 (the tensor-core K step): g in {1, 2, 4}. More
+row-parallel GEMM (`exchange="nccl"`), or, with `exchange="nvlink"`, none at all -- a
+reduce-scatter and an all-gather over NVLink peer memory (csrc/tp_exchange.cu): the GEMM's
+epilogue stores the tile rows of row block s into rank s's exchange buffer, a flag per rank
+marks them complete, rank s adds the bias and the g partials of its block to its residual stream
+in rank order and stores the sum into every rank's gather buffer, and a second round of flags
+lets each rank copy the other blocks in (the same sum, bit for bit, on every rank). g divides
+12 and the local widths (768/g and 3072/g) stay multiples of 64 (the tensor-core K step): g in
+{1, 2, 4}. More
 ranks than that run as data-parallel groups of tensor-parallel ranks (`hybrid_layout`,
 `hybrid_groups`): 8 GPUs as 2 groups of 4, each group with half the batch.
 """
@@ -83,7 +86,12 @@ def _bind_exchange(lib) -> None:
     lib.ppyb200_tp_partial_scatter.argtypes = [p, p, p, i32, i64, i64, i64, p]
     lib.ppyb200_tp_signal.argtypes = [p, i32, i32, i32]
     lib.ppyb200_tp_accumulate.argtypes = [p, p, p, p, i32, i64, i64, i32, p]
-    for name in ("ppyb200_tp_partial_scatter", "ppyb200_tp_signal", "ppyb200_tp_accumulate"):
+    lib.ppyb200_tp_partial_reduce_scatter.argtypes = [p, p, p, i32, i64, i64, i64, p]
+    lib.ppyb200_tp_reduce_block.argtypes = [p, p, p, p, p, i32, i32, i64, i64, i32, p]
+    lib.ppyb200_tp_gather_blocks.argtypes = [p, p, p, i32, i32, i64, i64, i32, p]
+    for name in ("ppyb200_tp_partial_scatter", "ppyb200_tp_signal", "ppyb200_tp_accumulate",
+                 "ppyb200_tp_partial_reduce_scatter", "ppyb200_tp_reduce_block",
+                 "ppyb200_tp_gather_blocks"):
         getattr(lib, name).restype = i32
     lib._exchange_bound = True
 
@@ -206,19 +214,23 @@ class GPT2TensorParallel:
     # ---------------------------------------------------------------- the NVLink exchange
 
     def _exchange_state(self, tokens: int) -> dict:
-        """Exchange buffers for `tokens` rows (two parities x one [tokens, width] f32 slot per
-        rank) and the flag arrays: this rank's, and every other rank's mapped here. Made by
-        all ranks of the group together."""
+        """Exchange buffers for `tokens` rows and the flag arrays: this rank's, and every other
+        rank's mapped here. Made by all ranks of the group together. One allocation per rank:
+        the exchange buffer (two parities x one [ceil(tokens / size), width] f32 slot per rank,
+        the partials of this rank's row block), then the gather buffer (the same shape: the
+        other ranks' summed blocks). The flag array holds the first round's flags at [0, 8)
+        and the second's at [8, 16)."""
         import torch.distributed as dist
 
         if self._nvlink is not None and self._nvlink["tokens"] == tokens:
             return self._nvlink
         self.close()
         lib, size, rank = self.lib, self.shard.size, self.shard.rank
-        slot = tokens * self.config.width
+        block_rows = -(-tokens // size)
+        slot = block_rows * self.config.width
         handle = (ctypes.c_uint8 * 64)()
         flag_handle = (ctypes.c_uint8 * 64)()
-        own = lib.ppyb200_shared_alloc(2 * size * slot * 4, handle)
+        own = lib.ppyb200_shared_alloc(2 * 2 * size * slot * 4, handle)
         flags = lib.ppyb200_shared_alloc(64, flag_handle)
         if not own or not flags:
             raise runtime.B200Error(f"exchange buffers: {runtime.last_error()}")
@@ -239,7 +251,8 @@ class GPT2TensorParallel:
         self._epoch = 0  # the flags start at 0
         self._nvlink = {"tokens": tokens, "slot": slot, "own": own, "flags": flags,
                         "buffers": buffers, "flag_arrays": flag_arrays,
-                        "flag_set": (ctypes.c_void_p * size)(*flag_arrays)}
+                        "first": (ctypes.c_void_p * size)(*flag_arrays),
+                        "second": (ctypes.c_void_p * size)(*[f + 32 for f in flag_arrays])}
         return self._nvlink
 
     def close(self) -> None:
@@ -261,21 +274,31 @@ class GPT2TensorParallel:
         self.lib.ppyb200_shared_free(state["flags"])
 
     def _row_parallel_nvlink(self, a, w, bias, x, tokens, k, st, what):
+        """The reduce-scatter form: partials of row block s to rank s, the owner sums its block
+        and sends it to every rank (csrc/tp_exchange.cu)."""
         state = self._exchange_state(tokens)
         size, rank, slot = self.shard.size, self.shard.rank, state["slot"]
         self._epoch += 1
         epoch, parity = self._epoch, self._epoch & 1
-        # this rank's slot, in parity `parity`, of every rank's buffer
+        c = self.config.width
+        exchange = 4 * parity * size * slot            # byte offsets in each rank's allocation
+        gather = 4 * (2 + parity) * size * slot
+        # this rank's slot, in parity `parity`, of every rank's exchange and gather buffers
         slots = (ctypes.c_void_p * size)(
-            *[b + 4 * (parity * size + rank) * slot for b in state["buffers"]])
+            *[b + exchange + 4 * rank * slot for b in state["buffers"]])
+        peers = (ctypes.c_void_p * size)(
+            *[b + gather + 4 * rank * slot for b in state["buffers"]])
         lib = self.lib
-        self._check(lib.ppyb200_tp_partial_scatter(a.data_ptr(), w.data_ptr(), slots, size,
-                                                   tokens, self.config.width, k, st), what)
-        self._check(lib.ppyb200_tp_signal(state["flag_set"], size, rank, epoch), what)
-        self._check(lib.ppyb200_tp_accumulate(x.data_ptr(), bias.data_ptr(),
-                                              state["own"] + 4 * parity * size * slot,
-                                              state["flags"], size, tokens, self.config.width,
-                                              epoch, st), what)
+        self._check(lib.ppyb200_tp_partial_reduce_scatter(a.data_ptr(), w.data_ptr(), slots,
+                                                          size, tokens, c, k, st), what)
+        self._check(lib.ppyb200_tp_signal(state["first"], size, rank, epoch), what)
+        self._check(lib.ppyb200_tp_reduce_block(x.data_ptr(), bias.data_ptr(),
+                                                state["own"] + exchange, peers, state["flags"],
+                                                size, rank, tokens, c, epoch, st), what)
+        self._check(lib.ppyb200_tp_signal(state["second"], size, rank, epoch), what)
+        self._check(lib.ppyb200_tp_gather_blocks(x.data_ptr(), state["own"] + gather,
+                                                 state["flags"] + 32, size, rank, tokens, c,
+                                                 epoch, st), what)
 
     def _row_parallel(self, a, w, bias, x, tokens, k, st, what):
         """x <- x + bias + sum over ranks of a_r @ w_r^T (rank 0 keeps x and the bias)."""

@@ -153,6 +153,62 @@ def test_exchange_kernels_with_two_ranks_on_one_gpu():
     assert torch.equal(xs[0], xs[1])
 
 
+def test_reduce_scatter_exchange_with_three_ranks_on_one_gpu():
+    """The reduce-scatter form, three ranks' steps one after the other on one stream (every
+    buffer on this GPU), over 301 rows (blocks of 101, 101, 99): each rank's x ends equal, bit
+    for bit, to the all-slot form's x + bias + p0 + p1 + p2."""
+    import ctypes
+
+    lib = _exchange_lib()
+    ranks, m, n, k = 3, 301, 768, 128
+    rows = (m + ranks - 1) // ranks
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = [torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16) for _ in range(ranks)]
+    w = [torch.randn(n, k, device="cuda", generator=g).to(torch.bfloat16) for _ in range(ranks)]
+    bias = torch.randn(n, device="cuda", generator=g)
+    x0 = torch.randn(m, n, device="cuda", generator=g)
+    exchange = [torch.zeros(ranks, rows, n, device="cuda") for _ in range(ranks)]
+    gather = [torch.zeros(ranks, rows, n, device="cuda") for _ in range(ranks)]
+    flags = [torch.zeros(16, dtype=torch.int32, device="cuda") for _ in range(ranks)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    first = (ctypes.c_void_p * ranks)(*[f.data_ptr() for f in flags])
+    second = (ctypes.c_void_p * ranks)(*[f.data_ptr() + 32 for f in flags])
+    for r in range(ranks):
+        slots = (ctypes.c_void_p * ranks)(*[e[r].data_ptr() for e in exchange])
+        assert lib.ppyb200_tp_partial_reduce_scatter(a[r].data_ptr(), w[r].data_ptr(), slots,
+                                                     ranks, m, n, k, status.data_ptr()) == 0
+        assert lib.ppyb200_tp_signal(first, ranks, r, 1) == 0
+    xs = [x0.clone() for _ in range(ranks)]
+    for r in range(ranks):
+        peers = (ctypes.c_void_p * ranks)(*[gt[r].data_ptr() for gt in gather])
+        assert lib.ppyb200_tp_reduce_block(xs[r].data_ptr(), bias.data_ptr(),
+                                           exchange[r].data_ptr(), peers, flags[r].data_ptr(),
+                                           ranks, r, m, n, 1, status.data_ptr()) == 0
+        assert lib.ppyb200_tp_signal(second, ranks, r, 1) == 0
+    for r in range(ranks):
+        assert lib.ppyb200_tp_gather_blocks(xs[r].data_ptr(), gather[r].data_ptr(),
+                                            flags[r].data_ptr() + 32, ranks, r, m, n, 1,
+                                            status.data_ptr()) == 0
+    # the all-slot form on the same operands
+    full = torch.zeros(ranks, m, n, device="cuda")
+    one = torch.zeros(16, dtype=torch.int32, device="cuda")
+    for r in range(ranks):
+        slots = (ctypes.c_void_p * ranks)(*([full[r].data_ptr()] * ranks))
+        assert lib.ppyb200_tp_partial_scatter(a[r].data_ptr(), w[r].data_ptr(), slots, 1, m, n,
+                                              k, status.data_ptr()) == 0
+    one[:ranks] = 1
+    want = x0.clone()
+    assert lib.ppyb200_tp_accumulate(want.data_ptr(), bias.data_ptr(), full.data_ptr(),
+                                     one.data_ptr(), ranks, m, n, 1, status.data_ptr()) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    parts = [(a[r].float() @ w[r].float().t()) for r in range(ranks)]
+    assert torch.allclose(want, x0 + (bias + parts[0] + parts[1] + parts[2]), rtol=1e-4,
+                          atol=1e-3)
+    for r in range(ranks):
+        assert torch.equal(xs[r], want), r
+
+
 def test_exchange_wait_gives_up_and_raises_the_status():
     """A flag that nothing raises: the accumulate's bounded wait (about 2 s) gives up, raises
     the status word to 2 and leaves x alone; the context stays usable."""
