@@ -1280,16 +1280,18 @@ inline cudaError_t launch_single(const __nv_bfloat16* a, const __nv_bfloat16* bt
 }
 
 // The tile width for an m x n x k product on `units` SMs (one CTA per tile) or CTA pairs, in
-// rows of `block_rows`: 192 when K is shallow, n is a whole number of 192-wide tiles and
-// fewer waves x width are needed than with 256 -- GPT-2's out projection (N = 768, K = 768):
-// 0.744 against 0.793 ms per forward at 32768 rows (7 waves of 192 against 6 of 256 on 74
-// CTA pairs). At deep K a 192-wide tile loads a third more operand bytes per MMA than a
-// 256-wide one and the loads set the pace: the proj layer (K = 3072) took 2.09 against 1.79
-// ms. Else 256.
+// rows of `block_rows`: 192 when n is a whole number of 192-wide tiles and fewer waves x width
+// are needed than with 256 -- GPT-2's out projection (N = 768, K = 768): 0.744 against 0.793
+// ms per forward at 32768 rows (7 waves of 192 against 6 of 256 on 74 CTA pairs). At deep K a
+// 192-wide tile loads a third more operand bytes per MMA than a 256-wide one and the loads set
+// the pace when several waves run (the proj layer, K = 3072, took 2.09 against 1.79 ms at
+// 32768 rows), so there 192 is taken only when the 256-wide tiles do not fill one wave: the
+// proj layer at 4096 rows (48 of 74 pairs busy with 256, 64 with 192). Else 256.
 inline int pick_tile_n(int64_t m, int64_t n, int64_t k, int64_t block_rows, int64_t units) {
-  if (k >= DEEP_K || n % 192 != 0 || units < 1) return BN;
+  if (n % 192 != 0 || units < 1) return BN;
   const int64_t rows = (m + block_rows - 1) / block_rows;
   const int64_t wide = rows * ((n + 255) / 256), narrow = rows * (n / 192);
+  if (k >= DEEP_K && (wide >= units || narrow > units)) return BN;
   const int64_t cost_wide = (wide + units - 1) / units * 256;
   const int64_t cost_narrow = (narrow + units - 1) / units * 192;
   return cost_narrow < cost_wide ? 192 : BN;
