@@ -26,6 +26,9 @@
 //              allocation
 //   warp 10    one thread: the MMAs of query tile 1 (a single issuer serialised the two tiles'
 //              waits: 4500 cycles per key tile against about 1500 of tensor-core work)
+//   warp 11    idle: it completes the third warpgroup, which gives its registers to the
+//              softmax warpgroups (setmaxnreg: 224 a thread for warps 0-7, 56 for 8-11, so
+//              that a 128-score row and its state stay in registers)
 // Shared-memory operands are all K-major with the 128-byte swizzle: Q and K straight from the
 // QKV projection output [tokens, 3 * width]; V from a transposed copy V^T [batch * heads * 64,
 // length] that the QKV projection's epilogue writes beside it (keys contiguous).
