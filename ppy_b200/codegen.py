@@ -1069,29 +1069,57 @@ def _abi_params(params: list) -> list[str]:
 PIPELINE_SLICE = 1 << 21
 
 
-def _elementwise_span(fn: P.TensorFunction, buffers: list, counts: dict) -> str | None:
-    """The element count N of a function that is elementwise over one symbolic length: one
-    binding of N from a buffer's length, no temporaries, every kernel a map over [N] of
-    contiguous (not viewed) operands, every buffer exactly N elements. Such a function gives
-    the same result run on contiguous slices of its buffers one at a time. None otherwise."""
+def _slices(fn: P.TensorFunction, buffers: list, counts: dict) -> tuple[str, dict] | None:
+    """How a function splits into independent slices along its one symbolic length: one
+    binding of a symbol R from a buffer's length, no temporaries, every kernel a map over [R]
+    or a row kernel over [R, C] of contiguous (not viewed) operands. Every buffer then holds
+    k * R elements for a constant k (k elements per index of R: 1 for a map, C for the rows of
+    a row kernel, 1 for a per-row result), and slices [r0, r0 + len) of R touch elements
+    [k r0, k (r0 + len)) of it only; or a constant count (a per-column operand such as a
+    layernorm's gamma), which every slice reads whole and no kernel writes. Returns ("sym_R",
+    {buffer: k, or None for a whole one}); None when the function does not split so."""
     if len(fn.bindings) != 1 or fn.temps or fn.dim_guards or not fn.kernels or not buffers:
         return None
     b = fn.bindings[0]
-    if P.numel(b.divisor) != (1, []) and P.numel(b.divisor) != (1, ()):
-        return None
-    n = f"(int64_t)1 * sym_{b.symbol}"
+    r = b.symbol
     for kernel in fn.kernels:
-        if kernel.kind != "map" or P.spell_count(kernel.shape) != n or len(kernel.shape) != 1:
+        if kernel.kind not in ("map", "row"):
+            return None
+        shape = tuple(kernel.shape)
+        if kernel.kind == "map" and shape != (r,):
+            return None
+        if kernel.kind == "row" and (len(shape) != 2 or shape[0] != r
+                                     or not isinstance(shape[1], int)):
             return None
         operands = list(kernel.inputs) + [o.operand for o in kernel.outputs]
-        for o in operands:
-            if getattr(o, "view", None) is not None:
-                return None
-            if getattr(o, "source", None) == "param" and P.spell_count(o.shape) != n:
-                return None
-    if any(counts.get(p.name) != n for p in buffers):
+        if any(getattr(o, "view", None) is not None for o in operands):
+            return None
+    factors: dict = {}
+    for p in buffers:
+        count = counts.get(p.name)
+        if count is None:
+            return None
+        constant, symbols = P.numel(_count_shape(p))
+        if symbols == (r,):
+            factors[p.name] = constant
+        elif symbols == () and p.role == "in":
+            factors[p.name] = None
+        else:
+            return None
+        if count != (P.spell_count((constant, r)) if symbols else P.spell_count((constant,))):
+            return None
+    if not any(k is not None for k in factors.values()):
         return None
-    return n
+    return f"sym_{r}", factors
+
+
+def _count_shape(p) -> tuple:
+    """The one shape a buffer is read or written with (the first when several agree)."""
+    shapes = list(p.read_shapes) + list(p.write_shapes)
+    first = tuple(shapes[0])
+    if any(P.numel(tuple(s)) != P.numel(first) for s in shapes[1:]):
+        return ("?", "?")
+    return first
 
 
 def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
@@ -1198,7 +1226,7 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
     D.append("}")
     src.exports.append("\n".join(D))
     # host ABI
-    span = _elementwise_span(fn, buffers, counts)
+    span = _slices(fn, buffers, counts)
     H = [f'extern "C" PPYB200_EXPORT int32_t {sym}({", ".join(_abi_params(fn.params) + ["int64_t* slot"])}) {{',
          "  ppyb200_bind_device();"]
     H += G
@@ -1215,34 +1243,45 @@ def _tensor_function(fn: P.TensorFunction, src: _Source) -> None:
         H.append(f"  if ({' || '.join(conds)}) status = PPY_STATUS_RAISED;")
     indent = "  "
     if span is not None:
-        # Elementwise over N: contiguous slices of the buffers are independent, so large calls
-        # go in slices of PIPELINE_SLICE elements over two streams -- slice s's copies in,
-        # kernel and copies out on stream s % 2 -- and the copy in of one slice overlaps the
-        # kernel and copy out of the one before (host-to-device and device-to-host are
-        # separate PCIe directions).
-        sym_n = f"sym_{fn.bindings[0].symbol}"
-        slice_args = ([f"d_{p.name} + off" for p in buffers] + ["len"]
-                      + [f"p_{p.name}" for p in scalars])
-        H.append(f"  if (status == PPY_STATUS_OK && {sym_n} >= 2 * (int64_t){PIPELINE_SLICE}) {{")
+        # Independent slices along R (a map's elements, a row kernel's rows): large calls go in
+        # slices of about PIPELINE_SLICE elements of the widest buffer, over two streams --
+        # slice s's copies in, kernel and copies out on stream s % 2 -- so that the copy in of
+        # one slice overlaps the kernel and copy out of the one before (host-to-device and
+        # device-to-host are separate PCIe directions). Whole operands (per-column vectors) go
+        # in first, before the side stream forks from the call's stream.
+        sym_n, factors = span
+        widest = max(k for k in factors.values() if k is not None)
+        rows = max(1, PIPELINE_SLICE // widest)
+        slice_args = ([f"d_{p.name} + off * (int64_t){factors[p.name]}"
+                       if factors[p.name] is not None else f"d_{p.name}" for p in buffers]
+                      + ["len"] + [f"p_{p.name}" for p in scalars])
+        H.append(f"  if (status == PPY_STATUS_OK && {sym_n} >= 2 * (int64_t){rows}) {{")
+        for p in buffers:
+            if factors[p.name] is None:
+                H.append(f"    if (status == PPY_STATUS_OK) status = ppyb200_copy_to_device("
+                         f"d_{p.name}, {p.name}_ptr, n_{p.name} * (int64_t)sizeof("
+                         f"{P.ctype(p.dtype)}));")
         H.append("    void* home = ppyb200_stream();")
         H.append("    void* side = nullptr;")
-        H.append("    status = ppyb200_fork(&side);")
+        H.append("    if (status == PPY_STATUS_OK) status = ppyb200_fork(&side);")
         H.append(f"    for (int64_t off = 0, k = 0; status == PPY_STATUS_OK && off < {sym_n}; "
-                 f"off += {PIPELINE_SLICE}, ++k) {{")
-        H.append(f"      const int64_t len = {sym_n} - off < (int64_t){PIPELINE_SLICE} ? "
-                 f"{sym_n} - off : (int64_t){PIPELINE_SLICE};")
+                 f"off += {rows}, ++k) {{")
+        H.append(f"      const int64_t len = {sym_n} - off < (int64_t){rows} ? "
+                 f"{sym_n} - off : (int64_t){rows};")
         H.append("      ppyb200_set_stream(k % 2 ? side : home);")
         for p in buffers:
-            if p.role in ("in", "inout"):
+            k = factors[p.name]
+            if k is not None and p.role in ("in", "inout"):
                 H.append(f"      if (status == PPY_STATUS_OK) status = ppyb200_copy_to_device("
-                         f"d_{p.name} + off, {p.name}_ptr + off, len * (int64_t)sizeof("
-                         f"{P.ctype(p.dtype)}));")
+                         f"d_{p.name} + off * (int64_t){k}, {p.name}_ptr + off * (int64_t){k}, "
+                         f"len * (int64_t){k} * (int64_t)sizeof({P.ctype(p.dtype)}));")
         H.append(f"      if (status == PPY_STATUS_OK) status = run_{sym}({', '.join(slice_args)});")
         for p in buffers:
-            if p.role in ("out", "inout"):
+            k = factors[p.name]
+            if k is not None and p.role in ("out", "inout"):
                 H.append(f"      if (status == PPY_STATUS_OK) status = ppyb200_copy_to_host("
-                         f"{p.name}_ptr + off, d_{p.name} + off, len * (int64_t)sizeof("
-                         f"{P.ctype(p.dtype)}));")
+                         f"{p.name}_ptr + off * (int64_t){k}, d_{p.name} + off * (int64_t){k}, "
+                         f"len * (int64_t){k} * (int64_t)sizeof({P.ctype(p.dtype)}));")
         H.append("    }")
         H.append("    ppyb200_set_stream(home);")
         H.append("    if (side != nullptr) { const int32_t joined = ppyb200_join(side); "

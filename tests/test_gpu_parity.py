@@ -157,6 +157,24 @@ def test_softmax_layernorm_full_size_against_the_oracle(rt):
     assert np.abs(y.mean(axis=1)).max() < 1e-4
 
 
+def test_softmax_layernorm_host_call_in_row_slices(rt):
+    """The host-memory call over 10 037 rows goes in slices of 2048 rows over two streams
+    (the last one ragged), gamma and beta copied whole first: the same bits as the device call
+    on the whole batch."""
+    module = _load(rt, "rows")
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((10_037, 1024), dtype=np.float32)
+    gamma = (1 + 0.02 * rng.standard_normal(1024)).astype(np.float32)
+    beta = (0.02 * rng.standard_normal(1024)).astype(np.float32)
+    out = np.zeros_like(x)
+    assert module.softmax_layernorm(x.ravel(), gamma, beta, out.ravel()).status == 0
+    tout = torch.empty(x.shape, device="cuda")
+    assert module.device.softmax_layernorm(torch.from_numpy(x).cuda(), torch.from_numpy(gamma).cuda(),
+                                           torch.from_numpy(beta).cuda(), tout).status == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(out, tout.cpu().numpy())
+
+
 # ---------------------------------------------------------------- small fixtures
 
 
